@@ -1,0 +1,379 @@
+#!/usr/bin/env python3
+"""Benchmark: Q4_RDNA group-64 GEMV decode-step weight stream on B200.
+
+Default workload (N=1): one Qwen3-8B decode step = 252 independent Q4 group-64
+GEMVs (36 layers x q/k/v/o/gate/up/down, batch 1, fresh N(0,1) activation per
+tensor), run as one multi-GEMV plan (one persistent kernel launch per step).
+The step streams 3.69 GB of packed weights, far more than L2 (126 MB), so no
+L2 flush is needed between steps.
+
+  value    aggregate HBM GB/s = algorithmic bytes of the step / device time
+  e2e      same metric through the public C ABI with pinned HOST buffers: every
+           step copies all 252 activations host->device and all outputs back
+  roofline dominant kernel (the plan kernel) vs MEASURED_PEAKS.json hbm_gbs
+  cpu_baseline  the reference's own CPU GEMV (reference_q4_rdna compiled from
+           its source into oracle/_ref) on the host cores, bounded sample
+
+--gpus N (under torchrun): every tensor's output rows are sharded over the N
+ranks (tensor parallel, rows in multiples of 32) and the y slices are gathered
+with one NCCL all-gather per step; total work is fixed (strong scaling).
+--impl reference: the reference CPU implementation alone on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "rdna-gfx1201-v0.1_b200")
+for _p in (REPO, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+FALLBACK_HBM_GBS = 6650.0
+METRIC = "Q4-g64 GEMV HBM GB/s (% of peak) and us per Qwen3-8B decode step, 1/2/4/8 B200"
+UNIT = "GB/s"
+
+
+def hbm_peak():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        return float(json.load(open(p))["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(workload: str):
+    """Per-launch DRAM bytes of the plan kernel from the committed ncu summary."""
+    p = os.path.join(REPO, "profiles", "q4_gemv_kernel_traffic.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        line = line.strip()
+        if line.startswith(workload + "="):
+            try:
+                return int(line.split("=", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.path is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            f = [c.strip() for c in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()) if rows else None}
+
+
+def cpu_count():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def reference_cpu_rate(budget_s: float, threads: int):
+    """The reference's CPU GEMV (reference_q4_rdna, q4rdna_gemv_bench.hip:189-211,
+    compiled unmodified from the reference file into oracle/_ref) run
+    concurrently on `threads` host threads, each on its own 12288 x 4096 tensor
+    (26.7 MB, so the working set exceeds the CPU caches), until `budget_s`
+    seconds have passed.  Falls back to the oracle port (bit-exact with it) when
+    oracle/_ref was not built.  Returns (GB/s, kind, threads, sample)."""
+    import numpy as np
+
+    import oracle
+    from q4rdna import synth
+
+    N, K = 12288, 4096
+    nbytes = N * K * 34 // 64 + 4 * K + 4 * N
+    pool = min(threads, 16)  # 16 x 26.7 MB distinct tensors: far above any CPU cache
+    tiles = [synth.tiles_np(N, K, 31 + i) for i in range(pool)]
+    xs = [synth.x_np(K, 1, 61 + i)[0] for i in range(threads)]
+    kind = "reference" if oracle.ref is not None else "port"
+    if kind == "reference":
+        fns = [oracle.RefBenchGemv(t) for t in tiles]
+        outs = [np.empty(N, np.float32) for _ in range(threads)]
+
+    def one(i):
+        if kind == "reference":
+            # one prepared tensor per pool slot; y buffers are per call site
+            ref = fns[i % pool]
+            xv = xs[i]
+            oracle.ref.q4ref_bench_run(ref._h, xv.ctypes.data_as(oracle._f32p), outs[i].ctypes.data_as(oracle._f32p))
+        else:
+            oracle.gemv_f32(tiles[i % pool], xs[i], N, K, threads=1, decode="refcpu")
+
+    def round_():
+        ts = [threading.Thread(target=one, args=(i,)) for i in range(threads)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+
+    round_()  # warm-up (page-in)
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        round_()
+        calls += threads
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    sample = (f"reference_q4_rdna 12288x4096 f32 GEMV, {calls} calls on {threads} threads "
+              f"({calls // threads} rounds, {el:.1f} s)")
+    if kind == "port":
+        sample = sample.replace("reference_q4_rdna", "oracle port of reference_q4_rdna")
+    return calls * nbytes / el / 1e9, kind, threads, sample
+
+
+def build_step(model: str, rank: int, world: int, device, seed: int):
+    """Weights (this rank's row shard of every tensor), activations and outputs
+    of one decode step, laid out so a step's inputs and outputs are each one
+    contiguous buffer (one copy each way for the end-to-end leg)."""
+    import torch
+
+    from q4rdna import synth
+
+    names = synth.model_tensors(model)
+    shards = []
+    for (n, N, K) in names:
+        if N % (32 * world):
+            raise SystemExit(f"{n}: {N} rows do not shard into {world} x 32-row slices")
+        shards.append((n, N // world, K))
+    xsz = sum(K for _, _, K in shards)
+    ysz = sum(n for _, n, _ in shards)
+    x_all = torch.empty(xsz, dtype=torch.float32, device=device)
+    y_all = torch.empty(ysz, dtype=torch.float32, device=device)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)  # same activations on every rank (replicated x)
+    x_all.normal_(generator=g)
+    descs, xo, yo = [], 0, 0
+    wbytes = abytes = 0
+    for i, (n, Ns, K) in enumerate(shards):
+        t = synth.tiles_torch(Ns, K, seed + 1 + i * world + rank, device)
+        descs.append({"tiles": t, "x": x_all[xo:xo + K].view(1, K), "y": y_all[yo:yo + Ns].view(1, Ns)})
+        xo += K
+        yo += Ns
+        wbytes += Ns * K * 34 // 64
+        abytes += Ns * K * 34 // 64 + 4 * K + 4 * Ns
+    return descs, x_all, y_all, wbytes, abytes, len(names)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import q4rdna
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if q4rdna.lib is None:
+        raise SystemExit("libq4rdna.so not built")
+
+    descs, x_all, y_all, wbytes, abytes, ntensors = build_step(args.model, rank, world, dev, args.seed)
+    plan = q4rdna.Plan(descs, B=1)
+    info = plan.info()
+    stream = torch.cuda.current_stream()
+    gathered = torch.empty(y_all.numel() * world, device=dev) if world > 1 else None
+
+    def step():
+        plan.run(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, y_all)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    k_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = q4rdna.launch_count()
+    with ClockSampler(local) as clk:
+        t0.record(stream)
+        for i in range(args.steps):
+            k_ev[i][0].record(stream)
+            plan.run(stream)
+            k_ev[i][1].record(stream)
+            if world > 1:
+                dist.all_gather_into_tensor(gathered, y_all)
+        t1.record(stream)
+        barrier()
+    launches = q4rdna.launch_count() - l0
+    ms_total = t0.elapsed_time(t1)
+    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in k_ev)
+
+    # end-to-end: pinned host activations in, outputs out, every step
+    x_host = torch.empty(x_all.numel(), dtype=torch.float32, pin_memory=True)
+    x_host.copy_(x_all)
+    y_host = torch.empty(y_all.numel() * world, dtype=torch.float32, pin_memory=True)
+    out_dev = gathered if world > 1 else y_all
+
+    def e2e_step():
+        x_all.copy_(x_host, non_blocking=True)
+        step()
+        y_host.copy_(out_dev, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+
+    # max over ranks (device-timed)
+    t = torch.tensor([ms_total, kern_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total, kern_ms, e2e_ms = t.tolist()
+    total_algo = abytes * world  # identical shard sizes on every rank
+    step_ms = ms_total / args.steps
+    peak, peak_kind = hbm_peak()
+    achieved = abytes / (kern_ms * 1e-3) / 1e9
+    out = None
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline:
+            v, kind, thr, sample = reference_cpu_rate(args.cpu_seconds, cpu_count())
+            cpu = {"value": round(v, 3), "unit": UNIT, "cores": thr, "kind": kind, "sample": sample}
+        out = {
+            "metric": METRIC, "value": round(total_algo / (step_ms * 1e-3) / 1e9, 2), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
+            "us_per_step": round(step_ms * 1e3, 2), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int4 x f32 (fp16 scales, f32 accumulate)",
+            "data": "synthetic: uniform int4 codes, fp16 scales |N(0,1)|*0.003, x ~ N(0,1) f32 (no Qwen3 weights offline)",
+            "config": {"workload": f"{args.model} decode-step weight stream: {ntensors} GEMVs batch 1"
+                                   + (f", rows sharded over {world} GPUs + NCCL all-gather" if world > 1 else ""),
+                       "tensors": ntensors, "batch": 1, "weight_bytes_per_step": wbytes * world,
+                       "algo_bytes_per_step": total_algo, "parallelism": f"tp{world}" if world > 1 else "none",
+                       "l2": "no flush: 3.69 GB streamed per step >> 126 MB L2",
+                       "plan_items": info["items"], "plan_grid": info["grid"]},
+            "e2e": {"value": round(total_algo / (e2e_ms / args.steps * 1e-3) / 1e9, 2), "unit": UNIT,
+                    "us_per_step": round(e2e_ms / args.steps * 1e3, 2),
+                    "h2d_bytes_per_step": x_all.numel() * 4, "d2h_bytes_per_step": y_host.numel() * 4},
+            "roofline": {"bound": "hbm", "kernel": "q4::q4_gemv_kernel<1> (plan)", "achieved": round(achieved, 1),
+                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "algo_bytes_per_launch": abytes, "kernel_us": round(kern_ms * 1e3, 2),
+                         "traffic": ncu_traffic(f"{args.model}_tp{world}")},
+            "cpu_baseline": cpu,
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+        }
+    plan.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    steps = []
+    thr = cpu_count()
+    for i in range(args.warmup + args.steps):
+        v, kind, thr, sample = reference_cpu_rate(args.ref_step_seconds, thr)
+        if i >= args.warmup:
+            steps.append(v)
+    v = statistics.mean(steps)
+    return {
+        "metric": METRIC, "impl": "reference", "value": round(v, 3), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32 (reference CPU GEMV)", "data": "synthetic, same distributions",
+        "config": {"workload": f"{args.model} decode-step weight stream (reference CPU GEMV on host cores)"},
+        "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": thr, "kind": kind, "sample": sample},
+        "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--model", choices=["qwen3-8b", "qwen3-32b"], default="qwen3-8b")
+    ap.add_argument("--seed", type=int, default=20260816)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--ref-step-seconds", type=float, default=4.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    out = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

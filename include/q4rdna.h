@@ -1,0 +1,189 @@
+/*
+ * q4rdna.h - C ABI of the B200 (sm_100a) Q4_RDNA group-64 decode GEMV.
+ *
+ * Plain pointers and sizes only.  Every device pointer is a CUDA device address
+ * on the current device; streams are cudaStream_t (declared here as an opaque
+ * pointer so the header needs no CUDA include).  All compute entry points are
+ * stream-ordered and never synchronise; they return a status and never abort.
+ *
+ * Weights use the reference's packed layout unchanged (32-row x 64-column
+ * tiles of 1088 bytes; see q4rdna_tile.h), so a tensor is N*K*34/64 bytes
+ * with N % 32 == 0 and K % 64 == 0.  Activations x are f32 [B][K] (column b at
+ * x + b*K); outputs y are f32 [B][N].
+ *
+ * Reference interfaces these replace (paths inside davidchen-rocm/RDNA-gfx1201-v0.1):
+ *   source/q4rdna.cuh:5-24       ggml_cuda_q4rdna_mul_mat / _mul_mat_add / _mul_mat_glu
+ *   source/q4rdna.cu:119-179     q4rdna_initialize (sidecar load + validation)
+ *   source/q4rdna.cu:578-680     q4rdna_launch and its split selector
+ *   source/q4rdna.cu:682-709     q4rdna_find / q4rdna_count (name registry, hits)
+ *   source/q4rdna.cu:73-112      launch counter and exit-time shape histogram
+ */
+#ifndef Q4RDNA_H
+#define Q4RDNA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default) /* the library builds with -fvisibility=hidden */
+#endif
+
+typedef struct CUstream_st *q4rdna_stream_t; /* == cudaStream_t */
+
+typedef enum q4rdna_status {
+    Q4RDNA_OK = 0,
+    Q4RDNA_ERR_INVALID_ARGUMENT = 1, /* null pointer, non-positive size, unknown op */
+    Q4RDNA_ERR_SHAPE = 2,            /* N % 32 != 0, K % 64 != 0, or shape mismatch */
+    Q4RDNA_ERR_ALIGNMENT = 3,        /* tiles not 16-byte aligned, x/y/add not 8-byte aligned */
+    Q4RDNA_ERR_WORKSPACE = 4,        /* workspace missing or smaller than q4rdna_workspace_bytes */
+    Q4RDNA_ERR_UNSUPPORTED = 5,      /* batch B outside [1, Q4RDNA_MAX_BATCH] */
+    Q4RDNA_ERR_CUDA = 6,             /* a CUDA call failed (launch, copy, allocation) */
+    Q4RDNA_ERR_IO = 7,               /* sidecar file missing, unreadable or truncated */
+    Q4RDNA_ERR_FORMAT = 8,           /* sidecar header or entry fails validation */
+    Q4RDNA_ERR_NOT_FOUND = 9,        /* tensor name not in the sidecar */
+    Q4RDNA_ERR_DEVICE = 10,          /* wrong or unavailable CUDA device */
+    Q4RDNA_ERR_TOO_LARGE = 11        /* size beyond a fixed limit of the entry point */
+} q4rdna_status;
+
+#define Q4RDNA_MAX_BATCH 16
+
+/* Which epilogue a GEMV applies (reference kernels' use_add / use_gate). */
+typedef enum q4rdna_op {
+    Q4RDNA_OP_PLAIN = 0,  /* y = W x                      (q4rdna.cu:713-745) */
+    Q4RDNA_OP_ADD = 1,    /* y = W x + add                (q4rdna.cu:747-767) */
+    Q4RDNA_OP_SWIGLU = 2  /* y = (W_up x) * silu(W_gate x) (q4rdna.cu:769-793) */
+} q4rdna_op;
+
+/* Launch options.  split = 0 lets the selector choose the split-K factor;
+ * split > 0 forces it (clamped to [1, K/64]). */
+typedef struct q4rdna_cfg {
+    int split;
+    int reserved[7];
+} q4rdna_cfg;
+
+const char *q4rdna_status_string(q4rdna_status s);
+/* Library version string. */
+const char *q4rdna_version(void);
+
+/* Split-K factor the selector would use for (N, K, B, op) on the current device. */
+int q4rdna_select_split(int N, int K, int B, int op);
+
+/* Device workspace a single GEMV needs: split-K partial sums plus arrival
+ * tickets.  0 when the chosen split is 1.  A workspace must be zero-filled once
+ * when it is allocated (q4rdna_workspace_init); every call leaves it zeroed
+ * again.  Calls that share a workspace must be ordered on one stream. */
+size_t q4rdna_workspace_bytes(int N, int K, int B, int op, const q4rdna_cfg *cfg);
+q4rdna_status q4rdna_workspace_init(void *workspace, size_t bytes, q4rdna_stream_t stream);
+
+/* y = W x.  Replaces the launch inside ggml_cuda_q4rdna_mul_mat
+ * (source/q4rdna.cu:736-741, q4rdna_launch<false,false>). */
+q4rdna_status q4rdna_gemv(const uint8_t *tiles, const float *x, float *y, int N, int K, int B,
+                          const q4rdna_cfg *cfg, void *workspace, size_t workspace_bytes,
+                          q4rdna_stream_t stream);
+
+/* y = W x + add, add f32 [B][N].  Replaces source/q4rdna.cu:760-763
+ * (q4rdna_launch<false,true>). */
+q4rdna_status q4rdna_gemv_add(const uint8_t *tiles, const float *x, const float *add, float *y,
+                              int N, int K, int B, const q4rdna_cfg *cfg, void *workspace,
+                              size_t workspace_bytes, q4rdna_stream_t stream);
+
+/* y = (W_up x) * silu(W_gate x), both tensors N x K, streamed by one kernel.
+ * Replaces source/q4rdna.cu:785-788 (q4rdna_launch<true,false>). */
+q4rdna_status q4rdna_gemv_swiglu(const uint8_t *up_tiles, const uint8_t *gate_tiles, const float *x,
+                                 float *y, int N, int K, int B, const q4rdna_cfg *cfg,
+                                 void *workspace, size_t workspace_bytes, q4rdna_stream_t stream);
+
+/* Debug: dense row-major W[N][K] = fp16 scale * int4 code, bit-exact (an fp16
+ * scale times an integer in [-8, 7] is exact in f32).  No reference
+ * counterpart; it is the dequantisation the reference kernels perform inline
+ * (source/q4rdna.cu:346-371). */
+q4rdna_status q4rdna_dequant_f32(const uint8_t *tiles, float *W, int N, int K, q4rdna_stream_t stream);
+
+/* ---- multi-GEMV plans: many independent GEMVs in one persistent launch ----
+ * One descriptor per GEMV; all share the batch B.  gate_tiles is used only by
+ * Q4RDNA_OP_SWIGLU, add only by Q4RDNA_OP_ADD.  The plan copies the
+ * descriptor table to the device once and owns its workspace; the caller keeps
+ * the buffers alive and rewrites x in place between runs.  No reference
+ * counterpart: the reference launches one kernel per mul_mat node. */
+typedef struct q4rdna_gemv_desc {
+    const uint8_t *tiles;
+    const uint8_t *gate_tiles;
+    const float *x;
+    const float *add;
+    float *y;
+    int N;
+    int K;
+    int op;
+    int split; /* 0 = selector */
+} q4rdna_gemv_desc;
+
+typedef struct q4rdna_plan q4rdna_plan;
+typedef struct q4rdna_plan_info {
+    int count;             /* GEMVs in the plan */
+    int batch;             /* B */
+    int64_t items;         /* warp work items per run */
+    int grid;              /* CTAs launched per run */
+    uint64_t weight_bytes; /* packed weight bytes streamed per run */
+    uint64_t algo_bytes;   /* weights + activations + outputs (+ add) per run */
+    size_t workspace_bytes;
+} q4rdna_plan_info;
+
+q4rdna_status q4rdna_plan_create(const q4rdna_gemv_desc *descs, int count, int B, q4rdna_plan **out);
+q4rdna_status q4rdna_plan_run(q4rdna_plan *plan, q4rdna_stream_t stream);
+q4rdna_status q4rdna_plan_get_info(const q4rdna_plan *plan, q4rdna_plan_info *info);
+void q4rdna_plan_destroy(q4rdna_plan *plan);
+
+/* ---- sidecar (the reference's .q4rdna container, byte layout unchanged) ----
+ * Header 48 B, entries 96 B, data at data_offset (source/q4rdna.cu:26-50).
+ * Validation follows source/q4rdna.cu:131-152.  The whole data region is
+ * uploaded to one device buffer owned by the handle. */
+typedef struct q4rdna_sidecar q4rdna_sidecar;
+
+q4rdna_status q4rdna_sidecar_open(const char *path, int device, q4rdna_sidecar **out);
+void q4rdna_sidecar_close(q4rdna_sidecar *sc);
+int q4rdna_sidecar_count(const q4rdna_sidecar *sc);
+q4rdna_status q4rdna_sidecar_entry(const q4rdna_sidecar *sc, int index, char name_out[64], int *rows,
+                                   int *cols, uint64_t *relative_offset);
+/* Device address of a tensor's tiles and its shape (q4rdna_find, q4rdna.cu:700-704). */
+q4rdna_status q4rdna_sidecar_find(const q4rdna_sidecar *sc, const char *name, int *rows, int *cols,
+                                  const uint8_t **tiles);
+
+/* ---- the reference's operator surface, keyed by ggml tensor name ----
+ * These carry the semantics of ggml_cuda_q4rdna_mul_mat / _mul_mat_add /
+ * _mul_mat_glu (source/q4rdna.cuh:5-24): return 1 when the work was enqueued on
+ * `stream`, 0 when the caller must use its stock kernel (sidecar unset, tensor
+ * out of scope or unknown, shape mismatch, other device).  The process-wide
+ * registry loads lazily from LLAMA_Q4_RDNA_SIDECAR on the first call, onto the
+ * device current at that call; LLAMA_Q4_RDNA_SCOPE (ffn | qkv-fallback |
+ * hotspot | attn) filters by name as in source/q4rdna.cu:685-696.
+ * weight_ne0 = K (columns) and weight_ne1 = N (rows) of the ggml weight tensor;
+ * x_ne0 must equal K and y_ne0 (elements of dst) must equal N.  Batch 1. */
+int q4rdna_mul_mat(const char *weight_name, int64_t weight_ne0, int64_t weight_ne1, const float *x,
+                   int64_t x_ne0, float *y, int64_t y_ne0, q4rdna_stream_t stream);
+int q4rdna_mul_mat_add(const char *weight_name, int64_t weight_ne0, int64_t weight_ne1, const float *x,
+                       int64_t x_ne0, const float *add, int64_t add_nelements, float *y,
+                       int64_t y_nelements, q4rdna_stream_t stream);
+int q4rdna_mul_mat_glu(const char *up_name, int64_t up_ne0, int64_t up_ne1, const char *gate_name,
+                       int64_t gate_ne0, int64_t gate_ne1, const float *x, int64_t x_ne0, float *y,
+                       int64_t y_nelements, q4rdna_stream_t stream);
+
+/* Counters (source/q4rdna.cu:73-112): kernels launched by this library, and per
+ * sidecar tensor the number of operator hits. */
+uint64_t q4rdna_launch_count(void);
+uint64_t q4rdna_registry_hits(const char *weight_name);
+/* Prints the reference's exit-time summary to stderr (also run at exit once the
+ * registry has loaded); LLAMA_Q4_RDNA_TRACE adds per-tensor hit lines. */
+void q4rdna_report_stats(void);
+/* Drops the process-wide registry (frees its device memory).  For tests. */
+void q4rdna_registry_reset(void);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+#endif /* Q4RDNA_H */

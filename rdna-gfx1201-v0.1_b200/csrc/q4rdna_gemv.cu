@@ -1,0 +1,781 @@
+// Q4_RDNA group-64 GEMV for B200 (sm_100a).
+//
+// One warp work item = one 128-row block (four 32-row tiles) x one K-range of
+// `Gs` groups, for one tensor (two for the fused SwiGLU).  The warp streams its
+// tiles straight from HBM with 128-bit loads, unpacks the int4 codes to fp16 in
+// registers and lets the tensor cores (mma.sync m16n8k16, f32 accumulate) do
+// the dot products against the activation, which is carried as an exact
+// fp16 hi + lo pair per element.  The fp16 group scale is applied once per
+// (row, group) in f32, as the reference does (source/q4rdna.cu:370-371).
+// Split-K partial sums go to a workspace; the last warp to finish a row block
+// (arrival ticket) adds them in split order and applies the add / SwiGLU
+// epilogue, so results are deterministic.
+//
+// Why tensor cores at batch 1: at 6.5 TB/s the stream is ~12e12 weights/s,
+// which leaves ~3 issue slots per weight on the CUDA cores.  Unpack + convert +
+// FFMA per weight does not fit; here the per-weight cost is ~1.1 integer/half
+// instructions plus 1/8 of an MMA issue.
+//
+// Register-fragment mapping (m16n8k16, A row-major, B col-major):
+//   lane L: grp = L>>2 (0..7), c = L&3; tile t = grp>>1, half h = grp&1.
+//   For MMA step m (0..7) the lane's 16-byte load is tile t, code bytes
+//   64 + 128m + 32c + 16h: rows 16h..16h+15 of column pair i = 4m + c.
+//   Its j-th 32-bit word (j = 0..3) holds rows rho = 16h + 4j + {0,1,2,3} and
+//   feeds MMA j.  Nibbles are expanded with the fp16 magic-number trick:
+//     P0 = (b0.lo, b2.lo), P1 = (b0.hi, b2.hi), P2 = (b1.lo, b3.lo), P3 = (b1.hi, b3.hi)
+//   and used as A registers a0a1 = P0, a2a3 = P2, a4a5 = P1, a6a7 = P3.  So MMA
+//   row grp carries weight rows rho+0 (even k-slots) and rho+2 (odd k-slots),
+//   MMA row grp+8 carries rho+1 / rho+3.  The B operand separates the two
+//   slots into different columns: column n = 4*bb + role, role 0/1 = slot 0
+//   (x_hi / x_lo), role 2/3 = slot 1 (x_hi / x_lo), bb = batch within the
+//   MMA's batch pair.  D column pairs (2c, 2c+1) therefore hold hi and lo for
+//   rows rho + 2(c&1) (+1 for the grp+8 half) of batch 2*nb + (c>>1).
+// Accumulation order of an output: inside a group the tensor core sums exact
+// products (int4 x fp16) in f32; groups of one split are added in ascending
+// order, each as sum = fma(scale * 2^e, hi + lo, sum); splits are then added
+// in ascending split order in f32.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <vector>
+
+#include "q4rdna.h"
+#include "q4rdna_tile.h"
+
+namespace q4 {
+
+constexpr int kWarps = 8;             // warps per CTA
+constexpr int kThreads = kWarps * 32;
+
+struct Task {
+    const uint8_t *w;   // primary tiles (W, or W_up for SwiGLU)
+    const uint8_t *w2;  // W_gate for SwiGLU, else null
+    const float *x;     // [B][K]
+    const float *add;   // [B][N] for OP_ADD, else null
+    float *y;           // [B][N]
+    float *part;        // [S][planes][B][N] split partials (S > 1)
+    unsigned *ticket;   // [RB] arrival counters (S > 1)
+    int N, K, G, RB, S, Gs, op, pad;
+    long long item_begin;
+};
+
+struct Launch {
+    const Task *table;  // device array of ntasks tasks, or null: use `one`
+    Task one;
+    int ntasks;
+    int B;
+    long long total_items;
+};
+
+// ---------------------------------------------------------------- device helpers
+
+__device__ __forceinline__ uint4 ld_stream16(const uint8_t *p) {
+    uint4 v;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+        : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t ld_stream4(const uint8_t *p) {
+    uint32_t v;
+    asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// (1024 + (n ^ 8)) - 1032 = signed code, exact in fp16.
+__device__ __forceinline__ uint32_t unbias_lo(uint32_t p) {
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(p), "r"(0x64086408u));
+    return r;
+}
+// (1024 + 16 (n ^ 8)) / 16 - 72 = signed code, exact in fp16.
+__device__ __forceinline__ uint32_t unbias_hi(uint32_t p) {
+    uint32_t r;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(p), "r"(0x2C002C00u), "r"(0xD480D480u));
+    return r;
+}
+
+// One 32-bit code word (4 rows x 1 column pair) -> the four A registers.
+__device__ __forceinline__ void word_to_a(uint32_t w, uint32_t &a0, uint32_t &a1, uint32_t &a2,
+                                          uint32_t &a3) {
+    const uint32_t w8 = w >> 8;
+    a0 = unbias_lo((w & 0x000F000Fu) ^ 0x64086408u);   // (b0.lo, b2.lo)
+    a1 = unbias_lo((w8 & 0x000F000Fu) ^ 0x64086408u);  // (b1.lo, b3.lo)
+    a2 = unbias_hi((w & 0x00F000F0u) ^ 0x64806480u);   // (b0.hi, b2.hi)
+    a3 = unbias_hi((w8 & 0x00F000F0u) ^ 0x64806480u);  // (b1.hi, b3.hi)
+}
+
+__device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Per-warp shared scratch: one group of the activation as (x_hi | x_lo << 16)
+// per element for each batch column of the pass, and the power of two that
+// undoes the group's normalisation.
+template <int NB>
+struct WarpSmem {
+    uint32_t xq[2 * NB][Q4_GROUP];
+    float up[2 * NB];
+};
+
+// Normalise one 64-element group of x by a power of two so that its largest
+// magnitude lands in [2^14, 2^15) (exact), then split every element into
+// x_hi = fp16(x) and x_lo = fp16(x - x_hi); x_hi + x_lo keeps ~22 significant
+// bits and the fp16 range can no longer overflow or underflow the group.
+__device__ __forceinline__ void prep_group(float2 v, uint32_t *xq_row, float *up, int lane) {
+    const float m = warp_max(fmaxf(fabsf(v.x), fabsf(v.y)));
+    float f = 1.0f, u = 1.0f;
+    if (m > 0.0f) {
+        const uint32_t e = max((__float_as_uint(m) >> 23) & 0xffu, 15u);
+        f = __uint_as_float((268u - e) << 23);  // 2^(141 - e)
+        u = __uint_as_float((e - 14u) << 23);   // 2^(e - 141)
+    }
+    const float s0 = v.x * f, s1 = v.y * f;
+    const __half2 hi = __floats2half2_rn(s0, s1);
+    const float2 hf = __half22float2(hi);
+    const __half2 lo = __floats2half2_rn(s0 - hf.x, s1 - hf.y);
+    const uint32_t hb = *reinterpret_cast<const uint32_t *>(&hi);
+    const uint32_t lb = *reinterpret_cast<const uint32_t *>(&lo);
+    uint2 q;
+    q.x = __byte_perm(hb, lb, 0x5410);  // element 2*lane:   hi | lo << 16
+    q.y = __byte_perm(hb, lb, 0x7632);  // element 2*lane+1
+    reinterpret_cast<uint2 *>(xq_row)[lane] = q;
+    if (lane == 0) *up = u;
+}
+
+// Code words and scale words of one (tensor, group) step for this lane.
+struct StepBuf {
+    uint4 q[8];     // MMA step m: 16 code bytes
+    uint32_t s[4];  // fp16 scale pair of the lane's two rows for MMA j
+};
+
+__device__ __forceinline__ void load_step(StepBuf &b, const uint8_t *tile, bool valid, int c, int h) {
+    if (valid) {
+        const uint8_t *qp = tile + Q4_SCALE_BYTES + 32 * c + 16 * h;
+#pragma unroll
+        for (int m = 0; m < 8; ++m) b.q[m] = ld_stream16(qp + 128 * m);
+        const uint8_t *sp = tile + 32 * h + 4 * (c & 1);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) b.s[j] = ld_stream4(sp + 8 * j);
+    } else {
+#pragma unroll
+        for (int m = 0; m < 8; ++m) b.q[m] = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) b.s[j] = 0u;
+    }
+}
+
+__device__ __forceinline__ uint32_t word_of(const uint4 &v, int j) {
+    return j == 0 ? v.x : (j == 1 ? v.y : (j == 2 ? v.z : v.w));
+}
+
+// One group of one tensor: 32 MMAs per warp (4 row slices x 8 k-steps x NB
+// batch pairs), then the per-(row, group) scale in f32.  While slot m of `buf`
+// is consumed it is refilled with slot m of the next step (`next`, when
+// non-null), so one step of loads stays in flight with one buffer of registers.
+template <int NB>
+__device__ __forceinline__ void compute_step(StepBuf &buf, const uint8_t *next, bool valid, int c, int h,
+                                             const WarpSmem<NB> &sm, float (&acc)[4][NB][2], int lane,
+                                             const uint32_t (&sel)[NB], const int (&xrow)[NB],
+                                             const int (&urow)[NB]) {
+    float D[4][NB][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) D[j][nb][r] = 0.0f;
+    uint32_t sw[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) sw[j] = buf.s[j];
+    const bool refill = next != nullptr && valid;
+    const uint8_t *nq = next + Q4_SCALE_BYTES + 32 * c + 16 * h;
+    if (refill) {
+        const uint8_t *sp = next + 32 * h + 4 * (c & 1);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) buf.s[j] = ld_stream4(sp + 8 * j);
+    }
+    const int c4 = lane & 3;
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+        const uint4 cur = buf.q[m];
+        if (refill) buf.q[m] = ld_stream16(nq + 128 * m);
+        uint32_t b0[NB], b1[NB];
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) {
+            const uint2 p = *reinterpret_cast<const uint2 *>(&sm.xq[xrow[nb]][8 * m + 2 * c4]);
+            b0[nb] = __byte_perm(p.x, 0u, sel[nb]);
+            b1[nb] = __byte_perm(p.y, 0u, sel[nb]);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint32_t a0, a1, a2, a3;
+            word_to_a(word_of(cur, j), a0, a1, a2, a3);
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb) mma16816(D[j][nb], a0, a1, a2, a3, b0[nb], b1[nb]);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float2 sc = __half22float2(*reinterpret_cast<const __half2 *>(&sw[j]));
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) {
+            const float u = sm.up[urow[nb]];
+            acc[j][nb][0] = fmaf(sc.x * u, D[j][nb][0] + D[j][nb][1], acc[j][nb][0]);
+            acc[j][nb][1] = fmaf(sc.y * u, D[j][nb][2] + D[j][nb][3], acc[j][nb][1]);
+        }
+    }
+}
+
+__device__ __forceinline__ float finish(float v, float gate, int op, const float *add, size_t idx) {
+    if (op == Q4RDNA_OP_ADD) v += add[idx];
+    if (op == Q4RDNA_OP_SWIGLU) v *= silu(gate);
+    return v;
+}
+
+// One work item: row block rb, split s of task T; NB batch pairs (B <= 2*NB).
+template <int NB, bool DUAL>
+__device__ __forceinline__ void run_item(const Task &T, long long local, int B, WarpSmem<NB> &sm, int lane) {
+    const int rb = (int)(local / T.S), s = (int)(local % T.S);
+    const int g0 = s * T.Gs, ng = min(T.Gs, T.G - g0);
+    const int grp = lane >> 2, c = lane & 3, t = grp >> 1, h = grp & 1;
+    const int tile_row = rb * Q4_BLOCK_TILES + t;
+    const bool valid = tile_row < (T.N >> 5);
+    const size_t tile0 = ((size_t)tile_row * T.G + g0) * Q4_TILE_BYTES;
+    const uint8_t *base0 = T.w + (valid ? tile0 : 0);
+    const uint8_t *base1 = DUAL ? T.w2 + (valid ? tile0 : 0) : nullptr;
+
+    // B operand selectors: lane's column is n = lane>>2 -> batch 2nb + (lane>>4), role (lane>>2)&3.
+    uint32_t sel[NB];
+    int xrow[NB], urow[NB];
+    {
+        const int role = (lane >> 2) & 3;
+        const uint32_t role_sel = role == 0 ? 0x4410u : role == 1 ? 0x4432u : role == 2 ? 0x1044u : 0x3244u;
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) {
+            const int bx = 2 * nb + (lane >> 4);
+            sel[nb] = bx < B ? role_sel : 0x4444u;
+            xrow[nb] = min(bx, B - 1);
+            urow[nb] = min(2 * nb + (c >> 1), B - 1);
+        }
+    }
+
+    float acc[DUAL ? 2 : 1][4][NB][2];
+#pragma unroll
+    for (int q = 0; q < (DUAL ? 2 : 1); ++q)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb) acc[q][j][nb][0] = acc[q][j][nb][1] = 0.0f;
+
+    // Activation of the first group; later groups are fetched one group ahead.
+    float2 xv[2 * NB];
+#pragma unroll
+    for (int b = 0; b < 2 * NB; ++b)
+        xv[b] = b < B ? __ldg(reinterpret_cast<const float2 *>(T.x + (size_t)b * T.K + (size_t)g0 * Q4_GROUP) + lane)
+                      : make_float2(0.0f, 0.0f);
+
+    const int nsteps = ng * (DUAL ? 2 : 1);
+    auto step_tile = [&](int st) -> const uint8_t * {
+        const int tt = DUAL ? (st & 1) : 0, gl = DUAL ? (st >> 1) : st;
+        return (tt ? base1 : base0) + (size_t)gl * Q4_TILE_BYTES;
+    };
+    StepBuf buf;
+    load_step(buf, step_tile(0), valid, c, h);
+    for (int st = 0; st < nsteps; ++st) {
+        const int tt = DUAL ? (st & 1) : 0, gl = DUAL ? (st >> 1) : st;
+        if (tt == 0) {
+            __syncwarp();
+#pragma unroll
+            for (int b = 0; b < 2 * NB; ++b)
+                if (b < B) prep_group(xv[b], sm.xq[b], &sm.up[b], lane);
+            if (gl + 1 < ng) {
+#pragma unroll
+                for (int b = 0; b < 2 * NB; ++b)
+                    if (b < B)
+                        xv[b] = __ldg(reinterpret_cast<const float2 *>(T.x + (size_t)b * T.K +
+                                                                       (size_t)(g0 + gl + 1) * Q4_GROUP) + lane);
+            }
+            __syncwarp();
+        }
+        const uint8_t *next = st + 1 < nsteps ? step_tile(st + 1) : nullptr;
+        if (DUAL && tt == 1)
+            compute_step<NB>(buf, next, valid, c, h, sm, acc[DUAL ? 1 : 0], lane, sel, xrow, urow);
+        else
+            compute_step<NB>(buf, next, valid, c, h, sm, acc[0], lane, sel, xrow, urow);
+    }
+
+    // Rows of this lane: tile t, rows 16h + 4j + 2(c&1) + e; batch 2nb + (c>>1).
+    const int row0 = tile_row * Q4_TILE_ROWS + 16 * h + 2 * (c & 1);
+    if (T.S == 1) {
+        if (valid) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int nb = 0; nb < NB; ++nb) {
+                    const int b = 2 * nb + (c >> 1);
+                    if (b >= B) continue;
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const size_t idx = (size_t)b * T.N + row0 + 4 * j + e;
+                        T.y[idx] = finish(acc[0][j][nb][e], acc[DUAL ? 1 : 0][j][nb][e], T.op, T.add, idx);
+                    }
+                }
+        }
+        return;
+    }
+
+    constexpr int planes = DUAL ? 2 : 1;
+    if (valid) {
+#pragma unroll
+        for (int q = 0; q < planes; ++q)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int nb = 0; nb < NB; ++nb) {
+                    const int b = 2 * nb + (c >> 1);
+                    if (b >= B) continue;
+#pragma unroll
+                    for (int e = 0; e < 2; ++e)
+                        __stcg(&T.part[(((size_t)s * planes + q) * B + b) * T.N + row0 + 4 * j + e], acc[q][j][nb][e]);
+                }
+    }
+    __threadfence();
+    __syncwarp();
+    unsigned prev = 0;
+    if (lane == 0) prev = atomicAdd(&T.ticket[rb], 1u);
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (prev != (unsigned)(T.S - 1)) return;
+
+    // Last arrival for this row block: add the splits in ascending order.
+    __threadfence();
+    for (int q4r = 0; q4r < Q4_BLOCK_TILES; ++q4r) {
+        const int row = rb * Q4_BLOCK_ROWS + 32 * q4r + lane;
+        if (row >= T.N) break;
+        for (int b = 0; b < B; ++b) {
+            float s0 = 0.0f, s1 = 0.0f;
+            const float *p0 = T.part + (size_t)b * T.N + row;
+            const size_t split_stride = (size_t)planes * B * T.N;
+#pragma unroll 8
+            for (int sp = 0; sp < T.S; ++sp) {
+                s0 += __ldcg(p0 + sp * split_stride);
+                if (DUAL) s1 += __ldcg(p0 + sp * split_stride + (size_t)B * T.N);
+            }
+            const size_t idx = (size_t)b * T.N + row;
+            T.y[idx] = finish(s0, s1, T.op, T.add, idx);
+        }
+    }
+    if (lane == 0) atomicExch(&T.ticket[rb], 0u);
+}
+
+__device__ __forceinline__ const Task &find_task(const Launch &L, long long item) {
+    if (L.table == nullptr) return L.one;
+    int lo = 0, hi = L.ntasks - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (L.table[mid].item_begin <= item) lo = mid; else hi = mid - 1;
+    }
+    return L.table[lo];
+}
+
+// Persistent over work items: warp w of the grid takes items w, w + nwarps, ...
+template <int NB>
+__global__ void __launch_bounds__(kThreads, NB == 1 ? 2 : 1) q4_gemv_kernel(const __grid_constant__ Launch L) {
+    __shared__ WarpSmem<NB> smem[kWarps];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long nw = (long long)gridDim.x * kWarps;
+    for (long long it = (long long)blockIdx.x * kWarps + warp; it < L.total_items; it += nw) {
+        const Task &T = find_task(L, it);
+        if (T.op == Q4RDNA_OP_SWIGLU)
+            run_item<NB, true>(T, it - T.item_begin, L.B, smem[warp], lane);
+        else
+            run_item<NB, false>(T, it - T.item_begin, L.B, smem[warp], lane);
+    }
+}
+
+// Debug dequantisation: one thread per (row, group) writes 64 exact values.
+__global__ void q4_dequant_kernel(const uint8_t *tiles, float *W, int N, int K) {
+    const long long G = K / Q4_GROUP;
+    const long long id = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (id >= (long long)N * G) return;
+    const long long row = id / G, g = id % G;
+    const uint8_t *t = tiles + ((row / Q4_TILE_ROWS) * G + g) * Q4_TILE_BYTES;
+    const int lane = (int)(row % Q4_TILE_ROWS);
+    const float s = __half2float(*reinterpret_cast<const __half *>(t + 2 * lane));
+    float *o = W + row * K + g * Q4_GROUP;
+    for (int i = 0; i < Q4_GROUP / 2; ++i) {
+        const uint8_t p = t[Q4_SCALE_BYTES + i * Q4_TILE_ROWS + lane];
+        o[2 * i] = s * (float)((int)(int8_t)(uint8_t)(p << 4) >> 4);
+        o[2 * i + 1] = s * (float)((int)(int8_t)p >> 4);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+
+constexpr int kMaxDevices = 64;
+constexpr int kMaxPassBatch = 4;  // batch columns per kernel pass (NB = 2)
+std::atomic<uint64_t> g_launches{0};
+
+struct DeviceInfo {
+    int sms = 0;
+    int occ[2] = {0, 0};  // resident CTAs per SM for NB = 1, 2
+};
+std::mutex g_dev_mutex;
+DeviceInfo g_dev[kMaxDevices];
+
+bool device_info(DeviceInfo &out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return false;
+    std::lock_guard<std::mutex> lock(g_dev_mutex);
+    DeviceInfo &d = g_dev[dev];
+    if (d.sms == 0) {
+        int sms = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return false;
+        int o1 = 0, o2 = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o1, q4_gemv_kernel<1>, kThreads, 0) != cudaSuccess ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o2, q4_gemv_kernel<2>, kThreads, 0) != cudaSuccess)
+            return false;
+        d.occ[0] = std::max(o1, 1);
+        d.occ[1] = std::max(o2, 1);
+        d.sms = sms;
+    }
+    out = d;
+    return true;
+}
+
+int env_split() {
+    // LLAMA_Q4_RDNA_COOP was the reference's split-K width (q4rdna.cu:578-589);
+    // here it forces the split-K factor.
+    const char *v = std::getenv("LLAMA_Q4_RDNA_COOP");
+    if (v == nullptr || *v == '\0') return 0;
+    const int s = std::atoi(v);
+    return s > 0 ? s : 0;
+}
+
+struct Split {
+    int S, Gs;
+};
+
+Split make_split(int G, int requested) {
+    requested = std::max(1, std::min(requested, G));
+    const int Gs = (G + requested - 1) / requested;
+    return Split{(G + Gs - 1) / Gs, Gs};
+}
+
+// Selector: enough work items to give every resident warp about one item.
+// The warp count comes from the live occupancy of this build; the per-shape
+// tuning table is measured separately and can override it through cfg/env.
+int select_split_for(int N, int K, int B, int op, const DeviceInfo &d) {
+    (void)op;
+    const int G = K / Q4_GROUP;
+    const int RB = (N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
+    const int nb_idx = std::min(B, kMaxPassBatch) <= 2 ? 0 : 1;
+    const long long warps = (long long)d.sms * d.occ[nb_idx] * kWarps;
+    long long S = (warps + RB - 1) / RB;
+    return make_split(G, (int)std::min<long long>(S, G)).S;
+}
+
+int resolve_split(int N, int K, int B, int op, const q4rdna_cfg *cfg, const DeviceInfo &d) {
+    const int G = K / Q4_GROUP;
+    int req = cfg != nullptr && cfg->split > 0 ? cfg->split : env_split();
+    if (req <= 0) req = select_split_for(N, K, B, op, d);
+    return make_split(G, req).S;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+size_t ws_bytes_for(int N, int B, int S, int op) {
+    if (S <= 1) return 0;
+    const int RB = (N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
+    const int planes = op == Q4RDNA_OP_SWIGLU ? 2 : 1;
+    const int pb = std::min(B, kMaxPassBatch);
+    return align256((size_t)RB * sizeof(unsigned)) + (size_t)S * planes * pb * N * sizeof(float);
+}
+
+bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+q4rdna_status check_shape(int N, int K, int B) {
+    if (N <= 0 || K <= 0) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    if (N % Q4_TILE_ROWS != 0 || K % Q4_GROUP != 0) return Q4RDNA_ERR_SHAPE;
+    if (B < 1 || B > Q4RDNA_MAX_BATCH) return Q4RDNA_ERR_UNSUPPORTED;
+    return Q4RDNA_OK;
+}
+
+q4rdna_status launch(const Launch &L, int grid, int nb, cudaStream_t stream) {
+    if (nb == 1)
+        q4_gemv_kernel<1><<<grid, kThreads, 0, stream>>>(L);
+    else
+        q4_gemv_kernel<2><<<grid, kThreads, 0, stream>>>(L);
+    if (cudaGetLastError() != cudaSuccess) return Q4RDNA_ERR_CUDA;
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return Q4RDNA_OK;
+}
+
+int grid_for(long long items, int nb, const DeviceInfo &d) {
+    const long long want = (items + kWarps - 1) / kWarps;
+    const long long cap = (long long)d.sms * d.occ[nb - 1];
+    return (int)std::max<long long>(1, std::min(want, cap));
+}
+
+q4rdna_status gemv_common(int op, const uint8_t *w, const uint8_t *w2, const float *x, const float *add, float *y,
+                          int N, int K, int B, const q4rdna_cfg *cfg, void *ws, size_t ws_bytes,
+                          cudaStream_t stream) {
+    q4rdna_status st = check_shape(N, K, B);
+    if (st != Q4RDNA_OK) return st;
+    if (w == nullptr || x == nullptr || y == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    if (op == Q4RDNA_OP_ADD && add == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    if (op == Q4RDNA_OP_SWIGLU && w2 == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    if (!aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(x, 8) || !aligned(y, 4) || (add && !aligned(add, 4)))
+        return Q4RDNA_ERR_ALIGNMENT;
+    DeviceInfo d;
+    if (!device_info(d)) return Q4RDNA_ERR_DEVICE;
+    const int G = K / Q4_GROUP;
+    const int RB = (N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
+    const Split sp = make_split(G, resolve_split(N, K, B, op, cfg, d));
+    unsigned *ticket = nullptr;
+    float *part = nullptr;
+    if (sp.S > 1) {
+        const size_t need = ws_bytes_for(N, B, sp.S, op);
+        if (ws == nullptr || ws_bytes < need || !aligned(ws, 256)) return Q4RDNA_ERR_WORKSPACE;
+        ticket = static_cast<unsigned *>(ws);
+        part = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + align256((size_t)RB * sizeof(unsigned)));
+    }
+    // Batches above kMaxPassBatch run in passes of up to 4 columns; every pass
+    // re-streams the weights (the tensor-core tile path for B >= 8 replaces this).
+    for (int b0 = 0; b0 < B; b0 += kMaxPassBatch) {
+        const int pb = std::min(kMaxPassBatch, B - b0);
+        Launch L{};
+        L.table = nullptr;
+        L.ntasks = 1;
+        L.B = pb;
+        Task &T = L.one;
+        T.w = w;
+        T.w2 = w2;
+        T.x = x + (size_t)b0 * K;
+        T.add = add ? add + (size_t)b0 * N : nullptr;
+        T.y = y + (size_t)b0 * N;
+        T.part = part;
+        T.ticket = ticket;
+        T.N = N; T.K = K; T.G = G; T.RB = RB; T.S = sp.S; T.Gs = sp.Gs; T.op = op; T.pad = 0;
+        T.item_begin = 0;
+        L.total_items = (long long)RB * sp.S;
+        const int nb = pb <= 2 ? 1 : 2;
+        st = launch(L, grid_for(L.total_items, nb, d), nb, stream);
+        if (st != Q4RDNA_OK) return st;
+    }
+    return Q4RDNA_OK;
+}
+
+}  // namespace q4
+
+using namespace q4;
+
+struct q4rdna_plan {
+    int device = -1;
+    int count = 0, B = 1, nb = 1, grid = 1;
+    long long items = 0;
+    Task *table = nullptr;     // device
+    void *workspace = nullptr; // device
+    size_t ws_bytes = 0;
+    uint64_t weight_bytes = 0, algo_bytes = 0;
+};
+
+extern "C" {
+
+const char *q4rdna_status_string(q4rdna_status s) {
+    switch (s) {
+        case Q4RDNA_OK: return "ok";
+        case Q4RDNA_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case Q4RDNA_ERR_SHAPE: return "unsupported shape (rows % 32, columns % 64)";
+        case Q4RDNA_ERR_ALIGNMENT: return "misaligned pointer";
+        case Q4RDNA_ERR_WORKSPACE: return "workspace missing or too small";
+        case Q4RDNA_ERR_UNSUPPORTED: return "unsupported batch";
+        case Q4RDNA_ERR_CUDA: return "CUDA error";
+        case Q4RDNA_ERR_IO: return "sidecar I/O error";
+        case Q4RDNA_ERR_FORMAT: return "invalid sidecar";
+        case Q4RDNA_ERR_NOT_FOUND: return "tensor not found";
+        case Q4RDNA_ERR_DEVICE: return "device error";
+        case Q4RDNA_ERR_TOO_LARGE: return "size beyond the entry point's limit";
+    }
+    return "unknown status";
+}
+
+const char *q4rdna_version(void) { return "q4rdna-b200 0.1 (sm_100a)"; }
+
+int q4rdna_select_split(int N, int K, int B, int op) {
+    if (check_shape(N, K, B) != Q4RDNA_OK) return 0;
+    DeviceInfo d;
+    if (!device_info(d)) return 0;
+    return resolve_split(N, K, B, op, nullptr, d);
+}
+
+size_t q4rdna_workspace_bytes(int N, int K, int B, int op, const q4rdna_cfg *cfg) {
+    if (check_shape(N, K, B) != Q4RDNA_OK) return 0;
+    DeviceInfo d;
+    if (!device_info(d)) return 0;
+    return ws_bytes_for(N, B, resolve_split(N, K, B, op, cfg, d), op);
+}
+
+q4rdna_status q4rdna_workspace_init(void *workspace, size_t bytes, q4rdna_stream_t stream) {
+    if (bytes == 0) return Q4RDNA_OK;
+    if (workspace == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    return cudaMemsetAsync(workspace, 0, bytes, (cudaStream_t)stream) == cudaSuccess ? Q4RDNA_OK : Q4RDNA_ERR_CUDA;
+}
+
+q4rdna_status q4rdna_gemv(const uint8_t *tiles, const float *x, float *y, int N, int K, int B,
+                          const q4rdna_cfg *cfg, void *workspace, size_t workspace_bytes, q4rdna_stream_t stream) {
+    return gemv_common(Q4RDNA_OP_PLAIN, tiles, nullptr, x, nullptr, y, N, K, B, cfg, workspace, workspace_bytes,
+                       (cudaStream_t)stream);
+}
+
+q4rdna_status q4rdna_gemv_add(const uint8_t *tiles, const float *x, const float *add, float *y, int N, int K, int B,
+                              const q4rdna_cfg *cfg, void *workspace, size_t workspace_bytes,
+                              q4rdna_stream_t stream) {
+    return gemv_common(Q4RDNA_OP_ADD, tiles, nullptr, x, add, y, N, K, B, cfg, workspace, workspace_bytes,
+                       (cudaStream_t)stream);
+}
+
+q4rdna_status q4rdna_gemv_swiglu(const uint8_t *up_tiles, const uint8_t *gate_tiles, const float *x, float *y,
+                                 int N, int K, int B, const q4rdna_cfg *cfg, void *workspace,
+                                 size_t workspace_bytes, q4rdna_stream_t stream) {
+    return gemv_common(Q4RDNA_OP_SWIGLU, up_tiles, gate_tiles, x, nullptr, y, N, K, B, cfg, workspace,
+                       workspace_bytes, (cudaStream_t)stream);
+}
+
+q4rdna_status q4rdna_dequant_f32(const uint8_t *tiles, float *W, int N, int K, q4rdna_stream_t stream) {
+    q4rdna_status st = check_shape(N, K, 1);
+    if (st != Q4RDNA_OK) return st;
+    if (tiles == nullptr || W == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    if (!aligned(tiles, 2) || !aligned(W, 4)) return Q4RDNA_ERR_ALIGNMENT;
+    const long long n = (long long)N * (K / Q4_GROUP);
+    q4_dequant_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(tiles, W, N, K);
+    if (cudaGetLastError() != cudaSuccess) return Q4RDNA_ERR_CUDA;
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return Q4RDNA_OK;
+}
+
+q4rdna_status q4rdna_plan_create(const q4rdna_gemv_desc *descs, int count, int B, q4rdna_plan **out) {
+    if (out == nullptr || descs == nullptr || count <= 0) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    if (B < 1 || B > kMaxPassBatch) return Q4RDNA_ERR_UNSUPPORTED;
+    DeviceInfo d;
+    if (!device_info(d)) return Q4RDNA_ERR_DEVICE;
+    std::vector<Task> host(count);
+    std::vector<size_t> ws_off(count);
+    size_t ws_total = 0;
+    long long items = 0;
+    uint64_t wbytes = 0, abytes = 0;
+    for (int i = 0; i < count; ++i) {
+        const q4rdna_gemv_desc &e = descs[i];
+        q4rdna_status st = check_shape(e.N, e.K, B);
+        if (st != Q4RDNA_OK) return st;
+        if (e.op < Q4RDNA_OP_PLAIN || e.op > Q4RDNA_OP_SWIGLU) return Q4RDNA_ERR_INVALID_ARGUMENT;
+        if (e.tiles == nullptr || e.x == nullptr || e.y == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
+        if (e.op == Q4RDNA_OP_ADD && e.add == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
+        if (e.op == Q4RDNA_OP_SWIGLU && e.gate_tiles == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
+        if (!aligned(e.tiles, 16) || (e.gate_tiles && !aligned(e.gate_tiles, 16)) || !aligned(e.x, 8) ||
+            !aligned(e.y, 4) || (e.add && !aligned(e.add, 4)))
+            return Q4RDNA_ERR_ALIGNMENT;
+        const int planes = e.op == Q4RDNA_OP_SWIGLU ? 2 : 1;
+        const int G = e.K / Q4_GROUP;
+        const int RB = (e.N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
+        // Plans hold many tensors, so items are sized by bytes (~64 KB of tiles)
+        // instead of by occupancy: split overhead stays ~1% of the stream.
+        int req = e.split;
+        if (req <= 0) {
+            const int gs = std::max(1, 65536 / (Q4_BLOCK_TILES * Q4_TILE_BYTES * planes));
+            req = (G + gs - 1) / gs;
+        }
+        const Split sp = make_split(G, req);
+        Task &T = host[i];
+        T.w = e.tiles; T.w2 = e.gate_tiles; T.x = e.x; T.add = e.add; T.y = e.y;
+        T.part = nullptr; T.ticket = nullptr;
+        T.N = e.N; T.K = e.K; T.G = G; T.RB = RB; T.S = sp.S; T.Gs = sp.Gs; T.op = e.op; T.pad = 0;
+        T.item_begin = items;
+        items += (long long)RB * sp.S;
+        ws_off[i] = ws_total;
+        ws_total += ws_bytes_for(e.N, B, sp.S, e.op);
+        wbytes += (uint64_t)planes * Q4_TENSOR_BYTES(e.N, e.K);
+        abytes += (uint64_t)planes * Q4_TENSOR_BYTES(e.N, e.K) + 4ull * e.K * B + 4ull * e.N * B +
+                  (e.op == Q4RDNA_OP_ADD ? 4ull * e.N * B : 0ull);
+    }
+    q4rdna_plan *p = new (std::nothrow) q4rdna_plan();
+    if (p == nullptr) return Q4RDNA_ERR_CUDA;
+    cudaGetDevice(&p->device);
+    if (ws_total > 0 && cudaMalloc(&p->workspace, ws_total) != cudaSuccess) { delete p; return Q4RDNA_ERR_CUDA; }
+    if (ws_total > 0 && cudaMemset(p->workspace, 0, ws_total) != cudaSuccess) { q4rdna_plan_destroy(p); return Q4RDNA_ERR_CUDA; }
+    for (int i = 0; i < count; ++i) {
+        Task &T = host[i];
+        if (T.S > 1) {
+            uint8_t *base = static_cast<uint8_t *>(p->workspace) + ws_off[i];
+            T.ticket = reinterpret_cast<unsigned *>(base);
+            T.part = reinterpret_cast<float *>(base + align256((size_t)T.RB * sizeof(unsigned)));
+        }
+    }
+    if (cudaMalloc(&p->table, sizeof(Task) * count) != cudaSuccess ||
+        cudaMemcpy(p->table, host.data(), sizeof(Task) * count, cudaMemcpyHostToDevice) != cudaSuccess) {
+        q4rdna_plan_destroy(p);
+        return Q4RDNA_ERR_CUDA;
+    }
+    p->count = count; p->B = B; p->nb = B <= 2 ? 1 : 2; p->items = items;
+    p->grid = grid_for(items, p->nb, d);
+    p->ws_bytes = ws_total; p->weight_bytes = wbytes; p->algo_bytes = abytes;
+    *out = p;
+    return Q4RDNA_OK;
+}
+
+q4rdna_status q4rdna_plan_run(q4rdna_plan *plan, q4rdna_stream_t stream) {
+    if (plan == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != plan->device) return Q4RDNA_ERR_DEVICE;
+    Launch L{};
+    L.table = plan->table;
+    L.ntasks = plan->count;
+    L.B = plan->B;
+    L.total_items = plan->items;
+    return launch(L, plan->grid, plan->nb, (cudaStream_t)stream);
+}
+
+q4rdna_status q4rdna_plan_get_info(const q4rdna_plan *plan, q4rdna_plan_info *info) {
+    if (plan == nullptr || info == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    info->count = plan->count;
+    info->batch = plan->B;
+    info->items = plan->items;
+    info->grid = plan->grid;
+    info->weight_bytes = plan->weight_bytes;
+    info->algo_bytes = plan->algo_bytes;
+    info->workspace_bytes = plan->ws_bytes;
+    return Q4RDNA_OK;
+}
+
+void q4rdna_plan_destroy(q4rdna_plan *plan) {
+    if (plan == nullptr) return;
+    if (plan->table) cudaFree(plan->table);
+    if (plan->workspace) cudaFree(plan->workspace);
+    delete plan;
+}
+
+uint64_t q4rdna_launch_count(void) { return g_launches.load(); }
+
+}  // extern "C"
