@@ -178,7 +178,7 @@ def reference_cpu_rate(budget_s: float, threads: int):
     return calls * nbytes / el / 1e9, kind, threads, sample
 
 
-def build_step(model: str, rank: int, world: int, device, seed: int):
+def build_step(model: str, rank: int, world: int, device, seed: int, layers: int = 0):
     """Weights (this rank's row shard of every tensor), activations and outputs
     of one decode step, laid out so a step's inputs and outputs are each one
     contiguous buffer (one copy each way for the end-to-end leg)."""
@@ -187,6 +187,8 @@ def build_step(model: str, rank: int, world: int, device, seed: int):
     from q4rdna import synth
 
     names = synth.model_tensors(model)
+    if layers:
+        names = [t for t in names if int(t[0].split(".")[1]) < layers]
     shards = []
     for (n, N, K) in names:
         if N % (32 * world):
@@ -231,7 +233,7 @@ def run_ours(args):
     if q4rdna.lib is None:
         raise SystemExit("libq4rdna.so not built")
 
-    descs, x_all, y_all, wbytes, abytes, ntensors = build_step(args.model, rank, world, dev, args.seed)
+    descs, x_all, y_all, wbytes, abytes, ntensors = build_step(args.model, rank, world, dev, args.seed, args.layers)
     plan = q4rdna.Plan(descs, B=1)
     info = plan.info()
     stream = torch.cuda.current_stream()
@@ -312,10 +314,11 @@ def run_ours(args):
             "scaling": "strong", "vs_baseline": None, "dtype": "int4 x f32 (fp16 scales, f32 accumulate)",
             "data": "synthetic: uniform int4 codes, fp16 scales |N(0,1)|*0.003, x ~ N(0,1) f32 (no Qwen3 weights offline)",
             "config": {"workload": f"{args.model} decode-step weight stream: {ntensors} GEMVs batch 1"
+                                   + (f" (first {args.layers} layers only)" if args.layers else "")
                                    + (f", rows sharded over {world} GPUs + NCCL all-gather" if world > 1 else ""),
                        "tensors": ntensors, "batch": 1, "weight_bytes_per_step": wbytes * world,
                        "algo_bytes_per_step": total_algo, "parallelism": f"tp{world}" if world > 1 else "none",
-                       "l2": "no flush: 3.69 GB streamed per step >> 126 MB L2",
+                       "l2": f"no flush: {wbytes * world / 1e9:.2f} GB streamed per step >> 126 MB L2",
                        "plan_items": info["items"], "plan_grid": info["grid"]},
             "e2e": {"value": round(total_algo / (e2e_ms / args.steps * 1e-3) / 1e9, 2), "unit": UNIT,
                     "us_per_step": round(e2e_ms / args.steps * 1e3, 2),
@@ -367,6 +370,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--ref-step-seconds", type=float, default=4.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="only the first L layers (small cases for profiling); 0 = the whole model")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

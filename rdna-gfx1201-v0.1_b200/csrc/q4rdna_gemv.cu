@@ -500,17 +500,33 @@ int resolve_split(int N, int K, int B, int op, const q4rdna_cfg *cfg, const Devi
     const int G = K / Q4_GROUP;
     int req = cfg != nullptr && cfg->split > 0 ? cfg->split : env_split();
     if (req <= 0) req = select_split_for(N, K, B, op, d);
+    if (N > (int)(65536 / sizeof(unsigned)) * Q4_BLOCK_ROWS) req = 1;
     return make_split(G, req).S;
 }
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
+// Single-call workspaces start with a fixed ticket area, so the partial sums of
+// any later call (any shape) never land on a ticket: every call leaves all
+// tickets at zero, which is the only state a call relies on.
+constexpr size_t kTicketArea = 65536;  // 16384 row blocks = 2,097,152 rows
+constexpr int kMaxSplitRows = (int)(kTicketArea / sizeof(unsigned)) * Q4_BLOCK_ROWS;
+
+size_t partial_bytes(int N, int B, int S, int op) {
+    const int planes = op == Q4RDNA_OP_SWIGLU ? 2 : 1;
+    return (size_t)S * planes * std::min(B, kMaxPassBatch) * N * sizeof(float);
+}
+
+// Workspace of one q4rdna_gemv* call: ticket area + partials (0 when S == 1).
 size_t ws_bytes_for(int N, int B, int S, int op) {
+    return S <= 1 ? 0 : kTicketArea + partial_bytes(N, B, S, op);
+}
+
+// Workspace of one plan task: its own tickets + partials (fixed for the plan's life).
+size_t plan_ws_bytes_for(int N, int B, int S, int op) {
     if (S <= 1) return 0;
     const int RB = (N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
-    const int planes = op == Q4RDNA_OP_SWIGLU ? 2 : 1;
-    const int pb = std::min(B, kMaxPassBatch);
-    return align256((size_t)RB * sizeof(unsigned)) + (size_t)S * planes * pb * N * sizeof(float);
+    return align256((size_t)RB * sizeof(unsigned)) + align256(partial_bytes(N, B, S, op));
 }
 
 bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
@@ -552,14 +568,15 @@ q4rdna_status gemv_common(int op, const uint8_t *w, const uint8_t *w2, const flo
     if (!device_info(d)) return Q4RDNA_ERR_DEVICE;
     const int G = K / Q4_GROUP;
     const int RB = (N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
-    const Split sp = make_split(G, resolve_split(N, K, B, op, cfg, d));
+    Split sp = make_split(G, resolve_split(N, K, B, op, cfg, d));
+    if (N > kMaxSplitRows) sp = make_split(G, 1);  // beyond the ticket area: no split
     unsigned *ticket = nullptr;
     float *part = nullptr;
     if (sp.S > 1) {
         const size_t need = ws_bytes_for(N, B, sp.S, op);
         if (ws == nullptr || ws_bytes < need || !aligned(ws, 256)) return Q4RDNA_ERR_WORKSPACE;
         ticket = static_cast<unsigned *>(ws);
-        part = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + align256((size_t)RB * sizeof(unsigned)));
+        part = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + kTicketArea);
     }
     // Batches above kMaxPassBatch run in passes of up to 4 columns; every pass
     // re-streams the weights (the tensor-core tile path for B >= 8 replaces this).
@@ -715,7 +732,7 @@ q4rdna_status q4rdna_plan_create(const q4rdna_gemv_desc *descs, int count, int B
         T.item_begin = items;
         items += (long long)RB * sp.S;
         ws_off[i] = ws_total;
-        ws_total += ws_bytes_for(e.N, B, sp.S, e.op);
+        ws_total += plan_ws_bytes_for(e.N, B, sp.S, e.op);
         wbytes += (uint64_t)planes * Q4_TENSOR_BYTES(e.N, e.K);
         abytes += (uint64_t)planes * Q4_TENSOR_BYTES(e.N, e.K) + 4ull * e.K * B + 4ull * e.N * B +
                   (e.op == Q4RDNA_OP_ADD ? 4ull * e.N * B : 0ull);

@@ -172,23 +172,29 @@ def test_plan_matches_oracle_and_is_deterministic(cuda):
         t = synth.tiles_np(N, K, 500 + i)
         g = synth.tiles_np(N, K, 600 + i) if op == 2 else None
         x = synth.x_np(K, 1, 700 + i)
+        a = synth.x_np(N, 1, 800 + i) if op == 1 else None
         d = {"tiles": to_dev(t, cuda), "x": to_dev(x, cuda), "y": torch.empty((1, N), device=cuda), "op": op}
         if op == 2:
             d["gate_tiles"] = to_dev(g, cuda)
+        if op == 1:
+            d["add"] = to_dev(a, cuda)
         descs.append(d)
-        host.append((t, g, x))
+        host.append((t, g, x, a))
     plan = q4rdna.Plan(descs, B=1)
     info = plan.info()
     assert info["count"] == len(specs) and info["items"] > 0
     plan.run()
     first = [d["y"].cpu().numpy().copy() for d in descs]
     plan.run()
-    for d, f, (N, K, op), (t, g, x) in zip(descs, first, specs, host):
+    for d, f, (N, K, op), (t, g, x, a) in zip(descs, first, specs, host):
         y = d["y"].cpu().numpy()
         assert np.array_equal(y.view(np.uint32), f.view(np.uint32))
         if op == 0:
             y64, mag = oracle.gemv_f64(t, x, N, K, threads=THREADS)
             tolerance.check(y, y64, mag, f"plan {N}x{K}")
+        elif op == 1:
+            y64, mag = oracle.gemv_f64(t, x, N, K, threads=THREADS)
+            tolerance.check(y, y64 + a, mag + np.abs(a), f"plan add {N}x{K}")
         else:
             yo = oracle.gemv_swiglu_f32(t, g, x, N, K, threads=THREADS)
             assert np.linalg.norm(y - yo) / np.linalg.norm(yo) <= 1e-5
@@ -264,3 +270,27 @@ def test_qwen3_8b_decode_step_plan_full_size(cuda):
         y64, mag = oracle.gemv_f64(t, x, N, K, threads=THREADS)
         tolerance.check(descs[i]["y"].cpu().numpy(), y64, mag, n)
     plan.close()
+
+
+def test_shared_workspace_across_shapes(cuda):
+    """One workspace reused by calls of growing row counts (the ticket area is
+    fixed, so a later call never reads an earlier call's partials as tickets)."""
+    import ctypes
+
+    L = q4rdna.lib
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    cfg = q4rdna.Cfg()
+    cfg.split = 2
+    shapes = [(4096, 12288), (12288, 4096), (1024, 4096), (25600, 5120)]
+    need = max(L.q4rdna_workspace_bytes(N, K, 1, 0, ctypes.byref(cfg)) for N, K in shapes)
+    ws = torch.zeros(need, dtype=torch.uint8, device=cuda)
+    for rep in range(2):
+        for i, (N, K) in enumerate(shapes):
+            tiles = synth.tiles_np(N, K, 300 + i)
+            x = synth.x_np(K, 1, 400 + i)
+            td, xd = to_dev(tiles, cuda), to_dev(x, cuda)
+            y = torch.empty(N, device=cuda)
+            assert L.q4rdna_gemv(td.data_ptr(), xd.data_ptr(), y.data_ptr(), N, K, 1, ctypes.byref(cfg),
+                                 ws.data_ptr(), need, st) == 0
+            y64, mag = oracle.gemv_f64(tiles, x, N, K, threads=THREADS)
+            tolerance.check(y.cpu().numpy(), y64, mag, f"shared ws {N}x{K} rep {rep}")
