@@ -96,6 +96,24 @@ q4rdna_status q4rdna_gemv_swiglu(const uint8_t *up_tiles, const uint8_t *gate_ti
                                  float *y, int N, int K, int B, const q4rdna_cfg *cfg,
                                  void *workspace, size_t workspace_bytes, q4rdna_stream_t stream);
 
+/* y = W x without any allocation and without a workspace argument.  No
+ * counterpart in the reference.  For callers that cannot call cudaMalloc: an
+ * operator hook inside a host framework (like the llama.cpp mul_mat hook) gets
+ * only its input and output tensors, device memory belongs to the framework's
+ * pool, and allocating there would stall the device and bypass the framework's
+ * memory accounting.  The split-K scratch is a fixed array of
+ * Q4RDNA_NOALLOC_SCRATCH_BYTES inside this library, held by every GPU that
+ * loads it until the process exits.  Calls whose split-K scratch would not fit
+ * return Q4RDNA_ERR_TOO_LARGE.  Results equal q4rdna_gemv's for the same cfg.
+ * The first call on a device looks up the array's device address (a one-time
+ * set-up per device); make that first call before any stream capture.  All
+ * calls on a device share the one array, so calls that overlap on the GPU (on
+ * different streams, or from several threads) race and must be serialised by
+ * the caller. */
+#define Q4RDNA_NOALLOC_SCRATCH_BYTES (8u << 20)
+q4rdna_status q4rdna_gemv_noalloc(const uint8_t *tiles, const float *x, float *y, int N, int K, int B,
+                                  const q4rdna_cfg *cfg, q4rdna_stream_t stream);
+
 /* Debug: dense row-major W[N][K] = fp16 scale * int4 code, bit-exact (an fp16
  * scale times an integer in [-8, 7] is exact in f32).  No reference
  * counterpart; it is the dequantisation the reference kernels perform inline

@@ -61,6 +61,7 @@ def _bind(lib):
         "q4rdna_gemv_add": (c_int, [P, P, P, P, c_int, c_int, c_int, POINTER(Cfg), P, c_size_t, P]),
         "q4rdna_gemv_swiglu": (c_int, [P, P, P, P, c_int, c_int, c_int, POINTER(Cfg), P, c_size_t, P]),
         "q4rdna_dequant_f32": (c_int, [P, P, c_int, c_int, P]),
+        "q4rdna_gemv_noalloc": (c_int, [P, P, P, c_int, c_int, c_int, POINTER(Cfg), P]),
         "q4rdna_plan_create": (c_int, [POINTER(GemvDesc), c_int, c_int, POINTER(P)]),
         "q4rdna_plan_run": (c_int, [P, P]),
         "q4rdna_plan_get_info": (c_int, [P, POINTER(PlanInfo)]),
@@ -90,6 +91,7 @@ lib = _bind(ctypes.CDLL(LIB_PATH)) if os.path.exists(LIB_PATH) else None
 SYMBOLS = [
     "q4rdna_status_string", "q4rdna_version", "q4rdna_select_split", "q4rdna_workspace_bytes",
     "q4rdna_workspace_init", "q4rdna_gemv", "q4rdna_gemv_add", "q4rdna_gemv_swiglu", "q4rdna_dequant_f32",
+    "q4rdna_gemv_noalloc",
     "q4rdna_plan_create", "q4rdna_plan_run", "q4rdna_plan_get_info", "q4rdna_plan_destroy",
     "q4rdna_sidecar_open", "q4rdna_sidecar_close", "q4rdna_sidecar_count", "q4rdna_sidecar_entry",
     "q4rdna_sidecar_find", "q4rdna_mul_mat", "q4rdna_mul_mat_add", "q4rdna_mul_mat_glu",
