@@ -192,6 +192,12 @@ int q4rdna_mul_mat_glu(const char *up_name, int64_t up_ne0, int64_t up_ne1, cons
  * sidecar tensor the number of operator hits. */
 uint64_t q4rdna_launch_count(void);
 uint64_t q4rdna_registry_hits(const char *weight_name);
+/* Device-side fault flags of the GEMV kernels since the last call, then cleared
+ * (synchronises the device).  Bit 0: a pipeline wait ran past its iteration
+ * limit (about 2 s), so the kernel stopped early and its outputs are invalid.
+ * 0 = no fault; 0xffffffff = the flag could not be read.  No reference
+ * counterpart (the reference kernels never wait). */
+uint32_t q4rdna_take_fault(void);
 /* Prints the reference's exit-time summary to stderr (also run at exit once the
  * registry has loaded); LLAMA_Q4_RDNA_TRACE adds per-tensor hit lines. */
 void q4rdna_report_stats(void);

@@ -134,7 +134,7 @@ __device__ __forceinline__ float warp_max(float v) {
 // per element for each batch column of the pass, and the power of two that
 // undoes the group's normalisation.
 template <int NB>
-struct WarpSmem {
+struct __align__(16) WarpSmem {
     uint32_t xq[2 * NB][Q4_GROUP];
     float up[2 * NB];
 };
@@ -254,6 +254,83 @@ __device__ __forceinline__ float finish(float v, float gate, int op, const float
     return v;
 }
 
+// Last warp to arrive at row block rb: add the split partials in ascending
+// split order, apply the epilogue, store y, and leave the ticket at zero.
+template <bool DUAL>
+__device__ __forceinline__ void reduce_splits(const Task &T, int rb, int B, int lane) {
+    constexpr int planes = DUAL ? 2 : 1;
+    __threadfence();
+    for (int q4r = 0; q4r < Q4_BLOCK_TILES; ++q4r) {
+        const int row = rb * Q4_BLOCK_ROWS + 32 * q4r + lane;
+        if (row >= T.N) break;
+        for (int b = 0; b < B; ++b) {
+            float s0 = 0.0f, s1 = 0.0f;
+            const float *p0 = T.part + (size_t)b * T.N + row;
+            const size_t split_stride = (size_t)planes * B * T.N;
+#pragma unroll 8
+            for (int sp = 0; sp < T.S; ++sp) {
+                s0 += __ldcg(p0 + sp * split_stride);
+                if (DUAL) s1 += __ldcg(p0 + sp * split_stride + (size_t)B * T.N);
+            }
+            const size_t idx = (size_t)b * T.N + row;
+            T.y[idx] = finish(s0, s1, T.op, T.add, idx);
+        }
+    }
+    if (lane == 0) atomicExch(&T.ticket[rb], 0u);
+}
+
+// Epilogue of one work item: store (S == 1), or write the split partials and,
+// in the last warp to arrive at the row block, add the splits in ascending
+// order and apply the add / SwiGLU epilogue.
+template <int NB, bool DUAL>
+__device__ __forceinline__ void finish_item(const Task &T, int rb, int s, int B,
+                                            float (&acc)[DUAL ? 2 : 1][4][NB][2], int lane, bool valid,
+                                            int tile_row, int h, int c) {
+    // Rows of this lane: tile t, rows 16h + 4j + 2(c&1) + e; batch 2nb + (c>>1).
+    const int row0 = tile_row * Q4_TILE_ROWS + 16 * h + 2 * (c & 1);
+    if (T.S == 1) {
+        if (valid) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int nb = 0; nb < NB; ++nb) {
+                    const int b = 2 * nb + (c >> 1);
+                    if (b >= B) continue;
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const size_t idx = (size_t)b * T.N + row0 + 4 * j + e;
+                        T.y[idx] = finish(acc[0][j][nb][e], acc[DUAL ? 1 : 0][j][nb][e], T.op, T.add, idx);
+                    }
+                }
+        }
+        return;
+    }
+
+    constexpr int planes = DUAL ? 2 : 1;
+    if (valid) {
+#pragma unroll
+        for (int q = 0; q < planes; ++q)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int nb = 0; nb < NB; ++nb) {
+                    const int b = 2 * nb + (c >> 1);
+                    if (b >= B) continue;
+#pragma unroll
+                    for (int e = 0; e < 2; ++e)
+                        __stcg(&T.part[(((size_t)s * planes + q) * B + b) * T.N + row0 + 4 * j + e], acc[q][j][nb][e]);
+                }
+    }
+    __threadfence();
+    __syncwarp();
+    unsigned prev = 0;
+    if (lane == 0) prev = atomicAdd(&T.ticket[rb], 1u);
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (prev != (unsigned)(T.S - 1)) return;
+
+    reduce_splits<DUAL>(T, rb, B, lane);
+}
+
 // One work item: row block rb, split s of task T; NB batch pairs (B <= 2*NB).
 template <int NB, bool DUAL>
 __device__ __forceinline__ void run_item(const Task &T, long long local, int B, WarpSmem<NB> &sm, int lane) {
@@ -326,67 +403,7 @@ __device__ __forceinline__ void run_item(const Task &T, long long local, int B, 
             compute_step<NB>(buf, next, valid, c, h, sm, acc[0], lane, sel, xrow, urow);
     }
 
-    // Rows of this lane: tile t, rows 16h + 4j + 2(c&1) + e; batch 2nb + (c>>1).
-    const int row0 = tile_row * Q4_TILE_ROWS + 16 * h + 2 * (c & 1);
-    if (T.S == 1) {
-        if (valid) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-#pragma unroll
-                for (int nb = 0; nb < NB; ++nb) {
-                    const int b = 2 * nb + (c >> 1);
-                    if (b >= B) continue;
-#pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        const size_t idx = (size_t)b * T.N + row0 + 4 * j + e;
-                        T.y[idx] = finish(acc[0][j][nb][e], acc[DUAL ? 1 : 0][j][nb][e], T.op, T.add, idx);
-                    }
-                }
-        }
-        return;
-    }
-
-    constexpr int planes = DUAL ? 2 : 1;
-    if (valid) {
-#pragma unroll
-        for (int q = 0; q < planes; ++q)
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-#pragma unroll
-                for (int nb = 0; nb < NB; ++nb) {
-                    const int b = 2 * nb + (c >> 1);
-                    if (b >= B) continue;
-#pragma unroll
-                    for (int e = 0; e < 2; ++e)
-                        __stcg(&T.part[(((size_t)s * planes + q) * B + b) * T.N + row0 + 4 * j + e], acc[q][j][nb][e]);
-                }
-    }
-    __threadfence();
-    __syncwarp();
-    unsigned prev = 0;
-    if (lane == 0) prev = atomicAdd(&T.ticket[rb], 1u);
-    prev = __shfl_sync(0xffffffffu, prev, 0);
-    if (prev != (unsigned)(T.S - 1)) return;
-
-    // Last arrival for this row block: add the splits in ascending order.
-    __threadfence();
-    for (int q4r = 0; q4r < Q4_BLOCK_TILES; ++q4r) {
-        const int row = rb * Q4_BLOCK_ROWS + 32 * q4r + lane;
-        if (row >= T.N) break;
-        for (int b = 0; b < B; ++b) {
-            float s0 = 0.0f, s1 = 0.0f;
-            const float *p0 = T.part + (size_t)b * T.N + row;
-            const size_t split_stride = (size_t)planes * B * T.N;
-#pragma unroll 8
-            for (int sp = 0; sp < T.S; ++sp) {
-                s0 += __ldcg(p0 + sp * split_stride);
-                if (DUAL) s1 += __ldcg(p0 + sp * split_stride + (size_t)B * T.N);
-            }
-            const size_t idx = (size_t)b * T.N + row;
-            T.y[idx] = finish(s0, s1, T.op, T.add, idx);
-        }
-    }
-    if (lane == 0) atomicExch(&T.ticket[rb], 0u);
+    finish_item<NB, DUAL>(T, rb, s, B, acc, lane, valid, tile_row, h, c);
 }
 
 __device__ __forceinline__ const Task &find_task(const Launch &L, long long item) {
@@ -431,15 +448,67 @@ __global__ void q4_dequant_kernel(const uint8_t *tiles, float *W, int N, int K) 
     }
 }
 
+#include "q4rdna_gemv_tma.cuh"
+#include "q4rdna_gemv_i8.cuh"
+
 // ------------------------------------------------------------------ host side
 
 constexpr int kMaxDevices = 64;
 constexpr int kMaxPassBatch = 4;  // batch columns per kernel pass (NB = 2)
 std::atomic<uint64_t> g_launches{0};
 
+// Kernel variants: the int8 tensor-core kernel, the fp16 register-load kernel,
+// or the fp16 TMA-ring kernel with one of four ring shapes.
+// Q4RDNA_KERNEL=i8|ldg|tmaA|tmaB|tmaC|tmaD selects one for A/B measurements; the
+// default is the fastest measured on B200.
+enum Variant { kI8 = 0, kLdg, kTmaA, kTmaB, kTmaC, kTmaD, kVariants };
+constexpr int kDefaultVariant = kI8;
+
+int variant() {
+    static const int v = [] {
+        const char *e = std::getenv("Q4RDNA_KERNEL");
+        if (e == nullptr || *e == '\0') return kDefaultVariant;
+        const char *names[kVariants] = {"i8", "ldg", "tmaA", "tmaB", "tmaC", "tmaD"};
+        for (int i = 0; i < kVariants; ++i)
+            if (std::strcmp(e, names[i]) == 0) return i;
+        return kDefaultVariant;
+    }();
+    return v;
+}
+
+struct KernelCfg {
+    const void *fn;
+    int threads, smem, warps;
+};
+
+// Batch class of a kernel pass: 0 -> 1 column, 1 -> 2 columns, 2 -> 3..4 columns.
+int batch_class(int pb) { return pb <= 1 ? 0 : (pb == 2 ? 1 : 2); }
+
+template <class R>
+KernelCfg tma_cfg(int pb) {
+    return pb <= 2 ? KernelCfg{(const void *)q4_gemv_tma_kernel<1, R>, R::THREADS, R::SMEM_BYTES, R::WARPS}
+                   : KernelCfg{(const void *)q4_gemv_tma_kernel<2, R>, R::THREADS, R::SMEM_BYTES, R::WARPS};
+}
+
+KernelCfg kernel_cfg(int v, int pb) {
+    switch (v) {
+        case kLdg:
+            return pb <= 2 ? KernelCfg{(const void *)q4_gemv_kernel<1>, kThreads, 0, kWarps}
+                           : KernelCfg{(const void *)q4_gemv_kernel<2>, kThreads, 0, kWarps};
+        case kTmaA: return tma_cfg<RingA>(pb);
+        case kTmaB: return tma_cfg<RingB>(pb);
+        case kTmaC: return tma_cfg<RingC>(pb);
+        case kTmaD: return tma_cfg<RingD>(pb);
+        default:
+            if (pb <= 1) return KernelCfg{(const void *)q4_gemv_i8_kernel<1>, kThreads, 0, kWarps};
+            if (pb == 2) return KernelCfg{(const void *)q4_gemv_i8_kernel<2>, kThreads, 0, kWarps};
+            return KernelCfg{(const void *)q4_gemv_i8_kernel<4>, kThreads, 0, kWarps};
+    }
+}
+
 struct DeviceInfo {
     int sms = 0;
-    int occ[2] = {0, 0};  // resident CTAs per SM for NB = 1, 2
+    int occ[kVariants][3] = {};  // resident CTAs per SM per variant and batch class (0: not yet known)
 };
 std::mutex g_dev_mutex;
 DeviceInfo g_dev[kMaxDevices];
@@ -452,13 +521,18 @@ bool device_info(DeviceInfo &out) {
     if (d.sms == 0) {
         int sms = 0;
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return false;
-        int o1 = 0, o2 = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o1, q4_gemv_kernel<1>, kThreads, 0) != cudaSuccess ||
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o2, q4_gemv_kernel<2>, kThreads, 0) != cudaSuccess)
-            return false;
-        d.occ[0] = std::max(o1, 1);
-        d.occ[1] = std::max(o2, 1);
         d.sms = sms;
+    }
+    const int v = variant();
+    for (int bc = 0; bc < 3; ++bc) {
+        if (d.occ[v][bc] != 0) continue;
+        const KernelCfg k = kernel_cfg(v, bc == 0 ? 1 : (bc == 1 ? 2 : 4));
+        if (k.smem > 48 * 1024 &&
+            cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem) != cudaSuccess)
+            return false;
+        int o = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k.fn, k.threads, k.smem) != cudaSuccess) return false;
+        d.occ[v][bc] = std::max(o, 1);
     }
     out = d;
     return true;
@@ -490,8 +564,9 @@ int select_split_for(int N, int K, int B, int op, const DeviceInfo &d) {
     (void)op;
     const int G = K / Q4_GROUP;
     const int RB = (N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
-    const int nb_idx = std::min(B, kMaxPassBatch) <= 2 ? 0 : 1;
-    const long long warps = (long long)d.sms * d.occ[nb_idx] * kWarps;
+    const int pb = std::min(B, kMaxPassBatch);
+    const long long warps =
+        (long long)d.sms * d.occ[variant()][batch_class(pb)] * kernel_cfg(variant(), pb).warps;
     long long S = (warps + RB - 1) / RB;
     return make_split(G, (int)std::min<long long>(S, G)).S;
 }
@@ -538,20 +613,23 @@ q4rdna_status check_shape(int N, int K, int B) {
     return Q4RDNA_OK;
 }
 
-q4rdna_status launch(const Launch &L, int grid, int nb, cudaStream_t stream) {
-    if (nb == 1)
-        q4_gemv_kernel<1><<<grid, kThreads, 0, stream>>>(L);
-    else
-        q4_gemv_kernel<2><<<grid, kThreads, 0, stream>>>(L);
+int grid_for(long long items, int pb, const DeviceInfo &d) {
+    const KernelCfg k = kernel_cfg(variant(), pb);
+    const long long want = (items + k.warps - 1) / k.warps;
+    const long long cap = (long long)d.sms * d.occ[variant()][batch_class(pb)];
+    return (int)std::max<long long>(1, std::min(want, cap));
+}
+
+// pb: batch columns of this pass (1..4).
+q4rdna_status launch(const Launch &L, int grid, int pb, cudaStream_t stream) {
+    const KernelCfg k = kernel_cfg(variant(), pb);
+    Launch arg = L;
+    void *args[] = {&arg};
+    if (cudaLaunchKernel(k.fn, dim3(grid), dim3(k.threads), args, (size_t)k.smem, stream) != cudaSuccess)
+        return Q4RDNA_ERR_CUDA;
     if (cudaGetLastError() != cudaSuccess) return Q4RDNA_ERR_CUDA;
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return Q4RDNA_OK;
-}
-
-int grid_for(long long items, int nb, const DeviceInfo &d) {
-    const long long want = (items + kWarps - 1) / kWarps;
-    const long long cap = (long long)d.sms * d.occ[nb - 1];
-    return (int)std::max<long long>(1, std::min(want, cap));
 }
 
 q4rdna_status gemv_common(int op, const uint8_t *w, const uint8_t *w2, const float *x, const float *add, float *y,
@@ -597,8 +675,7 @@ q4rdna_status gemv_common(int op, const uint8_t *w, const uint8_t *w2, const flo
         T.N = N; T.K = K; T.G = G; T.RB = RB; T.S = sp.S; T.Gs = sp.Gs; T.op = op; T.pad = 0;
         T.item_begin = 0;
         L.total_items = (long long)RB * sp.S;
-        const int nb = pb <= 2 ? 1 : 2;
-        st = launch(L, grid_for(L.total_items, nb, d), nb, stream);
+        st = launch(L, grid_for(L.total_items, pb, d), pb, stream);
         if (st != Q4RDNA_OK) return st;
     }
     return Q4RDNA_OK;
@@ -755,8 +832,8 @@ q4rdna_status q4rdna_plan_create(const q4rdna_gemv_desc *descs, int count, int B
         q4rdna_plan_destroy(p);
         return Q4RDNA_ERR_CUDA;
     }
-    p->count = count; p->B = B; p->nb = B <= 2 ? 1 : 2; p->items = items;
-    p->grid = grid_for(items, p->nb, d);
+    p->count = count; p->B = B; p->nb = B; p->items = items;
+    p->grid = grid_for(items, B, d);
     p->ws_bytes = ws_total; p->weight_bytes = wbytes; p->algo_bytes = abytes;
     *out = p;
     return Q4RDNA_OK;
@@ -794,5 +871,12 @@ void q4rdna_plan_destroy(q4rdna_plan *plan) {
 }
 
 uint64_t q4rdna_launch_count(void) { return g_launches.load(); }
+
+uint32_t q4rdna_take_fault(void) {
+    unsigned v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_fault, sizeof(v)) != cudaSuccess) return 0xffffffffu;
+    if (v != 0) cudaMemcpyToSymbol(g_fault, &zero, sizeof(zero));
+    return v;
+}
 
 }  // extern "C"

@@ -1,0 +1,344 @@
+// int8 tensor-core variant of the GEMV (included into q4rdna_gemv.cu inside
+// namespace q4).  Same work items and 128-bit load pattern as q4_gemv_kernel,
+// with fewer instructions per weight:
+//
+//   * codes: a nibble in the HIGH half of a byte is exactly 16 * code as an s8,
+//     so a 32-bit code word (4 rows x 2 columns) becomes two A registers with
+//     hi = w & 0xF0F0F0F0 and lo = (w << 4) & 0xF0F0F0F0: 3 integer ops per 8
+//     weights, no conversion and no offset to undo;
+//   * activation: per group, x is scaled by a power of two so its largest
+//     magnitude lies in [2^21, 2^22), rounded to an integer X (error <= 2^-22 of
+//     the group's largest |x|) and split exactly into three signed 8-bit limbs,
+//     X = L2 * 65536 + L1 * 256 + L0;
+//   * mma.sync m16n8k32 s8 x s8 -> s32 sums the products of one group exactly;
+//     the epilogue combines the limbs in f32 and applies scale * 2^e / 16 once
+//     per (row, group), as the reference applies its scale (q4rdna.cu:370-371).
+//
+// Fragment mapping (m16n8k32, A row-major, B col-major).  Lane (grp, c) loads,
+// for k-step m, 16 bytes of tile t = grp >> 1 at 64 + 128m + 32c + 16h
+// (h = grp & 1): words q0..q3 = rows 16h + 4j + {0..3} of column pair
+// i = 4m + c.  Row set r (r = 0, 1) uses q[2r] for MMA row grp and q[2r+1] for
+// MMA row grp + 8: A k-slots 4c + j hold the low-nibble column 2i of row
+// (16h + 8r + j [+4]), k-slots 16 + 4c + j the high-nibble column 2i + 1.  The
+// four rows of a register are separated by the B operand: for "MMA a" column
+// n = 2 * slot + limb carries limb L2 (limb 0) or L1 (limb 1) of x placed in
+// byte `slot` of the B register; for "MMA b" column 2 * slot + bb carries L0
+// of batch column 2p + bb.  So lane (grp, c) ends up holding, without any
+// shuffle, all three limb sums of rows 16h + c + {0, 4, 8, 12} of tile t.
+// Accumulation order: exact int32 inside a group; groups of a split in
+// ascending order as sum = fma(scale * 2^e / 16, hi_limbs + lo_limbs, sum);
+// splits in ascending order in f32 (finish_rows).
+
+template <int BB>
+struct __align__(16) I8Smem {
+    uint32_t xq[BB][Q4_GROUP];  // per k: L0 | L1 << 8 | L2 << 16 (s8 bytes)
+    float up[BB];               // 2^e: undoes the group's power-of-two scaling
+};
+
+// Signed byte 0 of v, sign-extended to 32 bits.
+__device__ __forceinline__ int sext8(int v) { return (int)(int8_t)(v & 0xff); }
+
+__device__ __forceinline__ uint32_t limbs_of(float xs) {
+    const int X = __float2int_rn(xs);
+    const int L0 = sext8(X);
+    const int X1 = (X - L0) >> 8;
+    const int L1 = sext8(X1);
+    const int L2 = (X1 - L1) >> 8;  // |X| <= 2^22 -> L2 in [-64, 64]
+    return ((uint32_t)L0 & 0xffu) | (((uint32_t)L1 & 0xffu) << 8) | (((uint32_t)L2 & 0xffu) << 16);
+}
+
+__device__ __forceinline__ void prep_group_i8(float2 v, uint32_t *xq_row, float *up, int lane) {
+    const float m = warp_max(fmaxf(fabsf(v.x), fabsf(v.y)));
+    float f = 1.0f, u = 1.0f;
+    if (m > 0.0f) {
+        // biased exponent E of the max: scale by 2^(148 - E) so max*scale < 2^22
+        const uint32_t e = max((__float_as_uint(m) >> 23) & 0xffu, 40u);
+        f = __uint_as_float((275u - e) << 23);
+        u = __uint_as_float((e - 21u) << 23);
+    }
+    uint2 w;
+    w.x = limbs_of(v.x * f);
+    w.y = limbs_of(v.y * f);
+    reinterpret_cast<uint2 *>(xq_row)[lane] = w;
+    if (lane == 0) *up = u;
+}
+
+__device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Number of "MMA b" instructions (L0 of two batch columns each) for BB columns.
+template <int BB>
+struct I8Shape {
+    static constexpr int NA = BB;             // "MMA a": L2, L1 of one batch column
+    static constexpr int NBP = (BB + 1) / 2;  // "MMA b": L0 of a batch pair
+};
+
+// B-operand selectors of this lane (fixed per kernel): byte `slot` of the
+// register takes limb byte `src` of the per-k word; all other bytes are zero.
+struct I8Sel {
+    uint32_t a;      // MMA a: src 2 (L2) or 1 (L1)
+    uint32_t b;      // MMA b: src 0 (L0), or all-zero when the batch is absent
+    int bcol_odd;    // MMA b: this lane's column carries batch 2p + 1
+};
+
+__device__ __forceinline__ uint32_t sel_one(int slot, int src) {
+    return (0x4444u & ~(0xFu << (4 * slot))) | ((uint32_t)src << (4 * slot));
+}
+
+// Code and scale words of one (tensor, group) step for this lane.
+struct StepBufI8 {
+    uint4 q[8];     // k-step m: 16 code bytes
+    uint32_t s[4];  // fp16 scale bits of rows 16h + c + 4q (low 16 bits)
+};
+
+__device__ __forceinline__ uint32_t ld_stream2(const uint8_t *p) {
+    unsigned short v;
+    asm("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
+}
+
+// Lane's address pieces inside a tile: codes at +64 + 32c + 16h (+128 m),
+// scales at +32h + 2c (+8 q).
+__device__ __forceinline__ void load_step_i8(StepBufI8 &b, const uint8_t *tile, int c, int h) {
+    const uint8_t *qp = tile + Q4_SCALE_BYTES + 32 * c + 16 * h;
+#pragma unroll
+    for (int m = 0; m < 8; ++m) b.q[m] = ld_stream16(qp + 128 * m);
+    const uint8_t *sp = tile + 32 * h + 2 * c;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) b.s[q] = ld_stream2(sp + 8 * q);
+}
+
+// One group of one tensor.  `next` is the tile of the step that follows (this
+// item's next step, the next item's first step, or this tile again at the very
+// end); slot m of `buf` is refilled from it as soon as it is consumed, so one
+// step of loads is always in flight and the loop has no branches.
+template <int BB>
+__device__ __forceinline__ void compute_step_i8(StepBufI8 &buf, const uint8_t *next, int c, int h,
+                                                const I8Smem<BB> &sm, float (&acc)[4][BB], int lane,
+                                                const I8Sel &sel) {
+    constexpr int NA = I8Shape<BB>::NA, NBP = I8Shape<BB>::NBP;
+    int D[2][NA + NBP][4];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int k = 0; k < NA + NBP; ++k)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) D[r][k][e] = 0;
+    uint32_t sw[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) sw[q] = buf.s[q];
+    {
+        const uint8_t *sp = next + 32 * h + 2 * c;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) buf.s[q] = ld_stream2(sp + 8 * q);
+    }
+    const uint8_t *nq = next + Q4_SCALE_BYTES + 32 * c + 16 * h;
+    const int c4 = lane & 3;
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+        const uint4 cur = buf.q[m];
+        buf.q[m] = ld_stream16(nq + 128 * m);
+        uint32_t ba0[NA], ba1[NA], bb0[NBP], bb1[NBP];
+        uint2 W[BB];
+#pragma unroll
+        for (int b = 0; b < BB; ++b) W[b] = *reinterpret_cast<const uint2 *>(&sm.xq[b][8 * m + 2 * c4]);
+#pragma unroll
+        for (int b = 0; b < NA; ++b) {
+            ba0[b] = __byte_perm(W[b].x, 0u, sel.a);
+            ba1[b] = __byte_perm(W[b].y, 0u, sel.a);
+        }
+#pragma unroll
+        for (int p = 0; p < NBP; ++p) {
+            // compile-time indices; the lane's odd/even column picks by select
+            const uint2 we = W[2 * p];
+            const uint2 wo = W[2 * p + 1 < BB ? 2 * p + 1 : 2 * p];
+            const bool odd = sel.bcol_odd != 0;
+            const uint32_t s = (odd && 2 * p + 1 >= BB) ? 0x4444u : sel.b;
+            bb0[p] = __byte_perm(odd ? wo.x : we.x, 0u, s);
+            bb1[p] = __byte_perm(odd ? wo.y : we.y, 0u, s);
+        }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const uint32_t wa = r == 0 ? cur.x : cur.z;  // rows 16h + 8r + {0..3}: MMA row grp
+            const uint32_t wb = r == 0 ? cur.y : cur.w;  // rows 16h + 8r + 4 + {0..3}: MMA row grp + 8
+            const uint32_t a0 = (wa << 4) & 0xF0F0F0F0u;  // 16 * low-nibble code (column 2i)
+            const uint32_t a1 = (wb << 4) & 0xF0F0F0F0u;
+            const uint32_t a2 = wa & 0xF0F0F0F0u;         // 16 * high-nibble code (column 2i + 1)
+            const uint32_t a3 = wb & 0xF0F0F0F0u;
+#pragma unroll
+            for (int b = 0; b < NA; ++b) imma16832(D[r][b], a0, a1, a2, a3, ba0[b], ba1[b]);
+#pragma unroll
+            for (int p = 0; p < NBP; ++p) imma16832(D[r][NA + p], a0, a1, a2, a3, bb0[p], bb1[p]);
+        }
+    }
+    // rows 16h + c + 4q, q = 2r + half: limb sums L2 = Da[2*half], L1 = Da[2*half+1],
+    // L0 = Db[2*half + (b & 1)]
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int r = q >> 1, hf = q & 1;
+        const float sc = __half2float(__ushort_as_half((unsigned short)sw[q])) * 0.0625f;
+#pragma unroll
+        for (int b = 0; b < BB; ++b) {
+            const int l2 = D[r][b][2 * hf], l1 = D[r][b][2 * hf + 1];
+            const int l0 = D[r][NA + (b >> 1)][2 * hf + (b & 1)];
+            const float v = fmaf((float)l2, 65536.0f, (float)(l1 * 256 + l0));
+            acc[q][b] = fmaf(sc * sm.up[b], v, acc[q][b]);
+        }
+    }
+}
+
+// Epilogue of one item in the int8 layout: lane rows tile_row*32 + 16h + c + 4q.
+template <int BB, bool DUAL>
+__device__ __forceinline__ void finish_rows_i8(const Task &T, int rb, int s, int B, float (&acc)[2][4][BB],
+                                               int lane, bool valid, int tile_row, int h, int c) {
+    const int row0 = tile_row * Q4_TILE_ROWS + 16 * h + c;
+    if (T.S == 1) {
+        if (valid) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+#pragma unroll
+                for (int b = 0; b < BB; ++b) {
+                    if (b >= B) continue;
+                    const size_t idx = (size_t)b * T.N + row0 + 4 * q;
+                    T.y[idx] = finish(acc[0][q][b], acc[DUAL ? 1 : 0][q][b], T.op, T.add, idx);
+                }
+        }
+        return;
+    }
+    constexpr int planes = DUAL ? 2 : 1;
+    if (valid) {
+#pragma unroll
+        for (int pl = 0; pl < planes; ++pl)
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+#pragma unroll
+                for (int b = 0; b < BB; ++b) {
+                    if (b >= B) continue;
+                    __stcg(&T.part[(((size_t)s * planes + pl) * B + b) * T.N + row0 + 4 * q], acc[pl][q][b]);
+                }
+    }
+    __threadfence();
+    __syncwarp();
+    unsigned prev = 0;
+    if (lane == 0) prev = atomicAdd(&T.ticket[rb], 1u);
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (prev != (unsigned)(T.S - 1)) return;
+    reduce_splits<DUAL>(T, rb, B, lane);
+}
+
+// This lane's tile of step 0 of an item, and the item's first group.  Rows past
+// N read the block's first row tile instead (always present), so every load is
+// in bounds and unconditional; those rows are never stored.
+__device__ __forceinline__ const uint8_t *item_tile0(const Task &T, int local, int lane, int *g0_out) {
+    const int rb = local / T.S, sp = local % T.S;
+    const int g0 = sp * T.Gs;
+    const int t = lane >> 3;
+    int tile_row = rb * Q4_BLOCK_TILES + t;
+    if (tile_row >= (T.N >> 5)) tile_row = rb * Q4_BLOCK_TILES;
+    if (g0_out) *g0_out = g0;
+    return T.w + ((size_t)tile_row * T.G + g0) * Q4_TILE_BYTES;
+}
+
+template <int BB, bool DUAL>
+__device__ __forceinline__ void run_item_i8(const Task &T, int local, int B, I8Smem<BB> &sm, int lane,
+                                            const I8Sel &sel, StepBufI8 &buf, float2 (&xv)[BB], const Task *nT,
+                                            int nlocal) {
+    const int rb = local / T.S, s = local % T.S;
+    const int g0 = s * T.Gs, ng = min(T.Gs, T.G - g0);
+    const int grp = lane >> 2, c = lane & 3, t = grp >> 1, h = grp & 1;
+    const int tile_row = rb * Q4_BLOCK_TILES + t;
+    const bool valid = tile_row < (T.N >> 5);
+    const uint8_t *base0 = item_tile0(T, local, lane, nullptr);
+    const uint8_t *base1 = DUAL ? T.w2 + (base0 - T.w) : base0;
+    int ng0 = 0;
+    const uint8_t *after = nT ? item_tile0(*nT, nlocal, lane, &ng0) : nullptr;
+    const int nsteps = ng * (DUAL ? 2 : 1);
+    if (after == nullptr)  // last item of this warp: re-read its last tile (in bounds, never used)
+        after = (DUAL ? base1 : base0) + (size_t)(ng - 1) * Q4_TILE_BYTES;
+
+    float acc[2][4][BB];
+#pragma unroll
+    for (int pl = 0; pl < 2; ++pl)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int b = 0; b < BB; ++b) acc[pl][q][b] = 0.0f;
+
+    for (int st = 0; st < nsteps; ++st) {
+        const int tt = DUAL ? (st & 1) : 0, gl = DUAL ? (st >> 1) : st;
+        if (tt == 0) {
+            __syncwarp();
+#pragma unroll
+            for (int b = 0; b < BB; ++b)
+                if (b < B) prep_group_i8(xv[b], sm.xq[b], &sm.up[b], lane);
+            // next group's activation: this item's, or the next item's first group
+#pragma unroll
+            for (int b = 0; b < BB; ++b) {
+                if (b >= B) continue;
+                if (gl + 1 < ng)
+                    xv[b] = __ldg(reinterpret_cast<const float2 *>(T.x + (size_t)b * T.K +
+                                                                   (size_t)(g0 + gl + 1) * Q4_GROUP) + lane);
+                else if (nT)
+                    xv[b] = __ldg(reinterpret_cast<const float2 *>(nT->x + (size_t)b * nT->K +
+                                                                   (size_t)ng0 * Q4_GROUP) + lane);
+            }
+            __syncwarp();
+        }
+        const uint8_t *next;
+        if (st + 1 < nsteps) {
+            const int tn = DUAL ? ((st + 1) & 1) : 0, gn = DUAL ? ((st + 1) >> 1) : st + 1;
+            next = (tn ? base1 : base0) + (size_t)gn * Q4_TILE_BYTES;
+        } else {
+            next = after;
+        }
+        if (DUAL && tt)
+            compute_step_i8<BB>(buf, next, c, h, sm, acc[1], lane, sel);
+        else
+            compute_step_i8<BB>(buf, next, c, h, sm, acc[0], lane, sel);
+    }
+    finish_rows_i8<BB, DUAL>(T, rb, s, B, acc, lane, valid, tile_row, h, c);
+}
+
+template <int BB>
+__global__ void __launch_bounds__(kThreads, BB <= 2 ? 2 : 1) q4_gemv_i8_kernel(const __grid_constant__ Launch L) {
+    __shared__ I8Smem<BB> smem[kWarps];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long nw = (long long)gridDim.x * kWarps;
+    long long it = (long long)blockIdx.x * kWarps + warp;
+    if (it >= L.total_items) return;
+    I8Sel sel;
+    {
+        const int n = lane >> 2;  // this lane's B column
+        sel.a = sel_one(n >> 1, (n & 1) ? 1 : 2);
+        sel.b = sel_one(n >> 1, 0);
+        sel.bcol_odd = n & 1;
+    }
+    const int c = lane & 3, h = (lane >> 2) & 1;
+    // Step 0 of the warp's first item and its first activation group.
+    StepBufI8 buf;
+    float2 xv[BB];
+    {
+        const Task &T = find_task(L, it);
+        int g0 = 0;
+        load_step_i8(buf, item_tile0(T, (int)(it - T.item_begin), lane, &g0), c, h);
+#pragma unroll
+        for (int b = 0; b < BB; ++b)
+            xv[b] = b < L.B ? __ldg(reinterpret_cast<const float2 *>(T.x + (size_t)b * T.K + (size_t)g0 * Q4_GROUP) + lane)
+                            : make_float2(0.0f, 0.0f);
+    }
+    for (; it < L.total_items; it += nw) {
+        const Task &T = find_task(L, it);
+        const long long nit = it + nw;
+        const Task *nT = nit < L.total_items ? &find_task(L, nit) : nullptr;
+        const int nlocal = nT ? (int)(nit - nT->item_begin) : 0;
+        if (T.op == Q4RDNA_OP_SWIGLU)
+            run_item_i8<BB, true>(T, (int)(it - T.item_begin), L.B, smem[warp], lane, sel, buf, xv, nT, nlocal);
+        else
+            run_item_i8<BB, false>(T, (int)(it - T.item_begin), L.B, smem[warp], lane, sel, buf, xv, nT, nlocal);
+    }
+}

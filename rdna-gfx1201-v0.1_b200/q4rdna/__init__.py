@@ -76,6 +76,7 @@ def _bind(lib):
         "q4rdna_mul_mat_glu": (c_int, [c_char_p, c_int64, c_int64, c_char_p, c_int64, c_int64, P, c_int64, P,
                                        c_int64, P]),
         "q4rdna_launch_count": (c_uint64, []),
+        "q4rdna_take_fault": (ctypes.c_uint32, []),
         "q4rdna_registry_hits": (c_uint64, [c_char_p]),
         "q4rdna_report_stats": (None, []),
         "q4rdna_registry_reset": (None, []),
@@ -95,7 +96,7 @@ SYMBOLS = [
     "q4rdna_plan_create", "q4rdna_plan_run", "q4rdna_plan_get_info", "q4rdna_plan_destroy",
     "q4rdna_sidecar_open", "q4rdna_sidecar_close", "q4rdna_sidecar_count", "q4rdna_sidecar_entry",
     "q4rdna_sidecar_find", "q4rdna_mul_mat", "q4rdna_mul_mat_add", "q4rdna_mul_mat_glu",
-    "q4rdna_launch_count", "q4rdna_registry_hits", "q4rdna_report_stats", "q4rdna_registry_reset",
+    "q4rdna_launch_count", "q4rdna_take_fault", "q4rdna_registry_hits", "q4rdna_report_stats", "q4rdna_registry_reset",
 ]
 
 
@@ -120,6 +121,11 @@ def check(st: int, what: str = "") -> None:
 
 def launch_count() -> int:
     return int(_lib().q4rdna_launch_count())
+
+
+def take_fault() -> int:
+    """Device fault flags since the last call (0 = none); synchronises the device."""
+    return int(_lib().q4rdna_take_fault())
 
 
 def _cfg(split: int):
