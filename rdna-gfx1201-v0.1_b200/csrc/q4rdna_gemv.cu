@@ -450,6 +450,7 @@ __global__ void q4_dequant_kernel(const uint8_t *tiles, float *W, int N, int K) 
 
 #include "q4rdna_gemv_tma.cuh"
 #include "q4rdna_gemv_i8.cuh"
+#include "q4rdna_gemv_i8_tma.cuh"
 
 // ------------------------------------------------------------------ host side
 
@@ -457,18 +458,17 @@ constexpr int kMaxDevices = 64;
 constexpr int kMaxPassBatch = 4;  // batch columns per kernel pass (NB = 2)
 std::atomic<uint64_t> g_launches{0};
 
-// Kernel variants: the int8 tensor-core kernel, the fp16 register-load kernel,
-// or the fp16 TMA-ring kernel with one of four ring shapes.
-// Q4RDNA_KERNEL=i8|ldg|tmaA|tmaB|tmaC|tmaD selects one for A/B measurements; the
-// default is the fastest measured on B200.
-enum Variant { kI8 = 0, kLdg, kTmaA, kTmaB, kTmaC, kTmaD, kVariants };
+// Kernel variants: the int8 tensor-core kernel with register loads (default,
+// fastest measured), the same math fed by a TMA ring, or the fp16 tensor-core
+// kernel.  Q4RDNA_KERNEL=i8|i8tma|ldg selects one for A/B measurements.
+enum Variant { kI8 = 0, kI8Tma, kLdg, kVariants };
 constexpr int kDefaultVariant = kI8;
 
 int variant() {
     static const int v = [] {
         const char *e = std::getenv("Q4RDNA_KERNEL");
         if (e == nullptr || *e == '\0') return kDefaultVariant;
-        const char *names[kVariants] = {"i8", "ldg", "tmaA", "tmaB", "tmaC", "tmaD"};
+        const char *names[kVariants] = {"i8", "i8tma", "ldg"};
         for (int i = 0; i < kVariants; ++i)
             if (std::strcmp(e, names[i]) == 0) return i;
         return kDefaultVariant;
@@ -484,31 +484,34 @@ struct KernelCfg {
 // Batch class of a kernel pass: 0 -> 1 column, 1 -> 2 columns, 2 -> 3..4 columns.
 int batch_class(int pb) { return pb <= 1 ? 0 : (pb == 2 ? 1 : 2); }
 
-template <class R>
-KernelCfg tma_cfg(int pb) {
-    return pb <= 2 ? KernelCfg{(const void *)q4_gemv_tma_kernel<1, R>, R::THREADS, R::SMEM_BYTES, R::WARPS}
-                   : KernelCfg{(const void *)q4_gemv_tma_kernel<2, R>, R::THREADS, R::SMEM_BYTES, R::WARPS};
+template <bool DUAL>
+KernelCfg i8_cfg(int pb) {
+    if (pb <= 1) return KernelCfg{(const void *)q4_gemv_i8_kernel<1, DUAL>, kThreads, 0, kWarps};
+    if (pb == 2) return KernelCfg{(const void *)q4_gemv_i8_kernel<2, DUAL>, kThreads, 0, kWarps};
+    return KernelCfg{(const void *)q4_gemv_i8_kernel<4, DUAL>, kThreads, 0, kWarps};
 }
 
-KernelCfg kernel_cfg(int v, int pb) {
+KernelCfg i8tma_cfg(int pb) {
+    using R = I8Ring;
+    if (pb <= 1) return KernelCfg{(const void *)q4_gemv_i8_tma_kernel<1, R>, R::THREADS, R::SMEM_BYTES, R::WARPS};
+    if (pb == 2) return KernelCfg{(const void *)q4_gemv_i8_tma_kernel<2, R>, R::THREADS, R::SMEM_BYTES, R::WARPS};
+    return KernelCfg{(const void *)q4_gemv_i8_tma_kernel<4, R>, R::THREADS, R::SMEM_BYTES, R::WARPS};
+}
+
+// dual: the launch holds a SwiGLU task (kernels without the SwiGLU path need fewer registers).
+KernelCfg kernel_cfg(int v, int pb, bool dual = true) {
     switch (v) {
+        case kI8Tma: return i8tma_cfg(pb);
         case kLdg:
             return pb <= 2 ? KernelCfg{(const void *)q4_gemv_kernel<1>, kThreads, 0, kWarps}
                            : KernelCfg{(const void *)q4_gemv_kernel<2>, kThreads, 0, kWarps};
-        case kTmaA: return tma_cfg<RingA>(pb);
-        case kTmaB: return tma_cfg<RingB>(pb);
-        case kTmaC: return tma_cfg<RingC>(pb);
-        case kTmaD: return tma_cfg<RingD>(pb);
-        default:
-            if (pb <= 1) return KernelCfg{(const void *)q4_gemv_i8_kernel<1>, kThreads, 0, kWarps};
-            if (pb == 2) return KernelCfg{(const void *)q4_gemv_i8_kernel<2>, kThreads, 0, kWarps};
-            return KernelCfg{(const void *)q4_gemv_i8_kernel<4>, kThreads, 0, kWarps};
+        default: return dual ? i8_cfg<true>(pb) : i8_cfg<false>(pb);
     }
 }
 
 struct DeviceInfo {
     int sms = 0;
-    int occ[kVariants][3] = {};  // resident CTAs per SM per variant and batch class (0: not yet known)
+    int occ[kVariants][3][2] = {};  // resident CTAs per SM: variant, batch class, SwiGLU (0: unknown)
 };
 std::mutex g_dev_mutex;
 DeviceInfo g_dev[kMaxDevices];
@@ -524,16 +527,18 @@ bool device_info(DeviceInfo &out) {
         d.sms = sms;
     }
     const int v = variant();
-    for (int bc = 0; bc < 3; ++bc) {
-        if (d.occ[v][bc] != 0) continue;
-        const KernelCfg k = kernel_cfg(v, bc == 0 ? 1 : (bc == 1 ? 2 : 4));
-        if (k.smem > 48 * 1024 &&
-            cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem) != cudaSuccess)
-            return false;
-        int o = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k.fn, k.threads, k.smem) != cudaSuccess) return false;
-        d.occ[v][bc] = std::max(o, 1);
-    }
+    for (int bc = 0; bc < 3; ++bc)
+        for (int du = 0; du < 2; ++du) {
+            if (d.occ[v][bc][du] != 0) continue;
+            const KernelCfg k = kernel_cfg(v, bc == 0 ? 1 : (bc == 1 ? 2 : 4), du != 0);
+            if (k.smem > 48 * 1024 &&
+                cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem) != cudaSuccess)
+                return false;
+            int o = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k.fn, k.threads, k.smem) != cudaSuccess)
+                return false;
+            d.occ[v][bc][du] = std::max(o, 1);
+        }
     out = d;
     return true;
 }
@@ -565,8 +570,9 @@ int select_split_for(int N, int K, int B, int op, const DeviceInfo &d) {
     const int G = K / Q4_GROUP;
     const int RB = (N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
     const int pb = std::min(B, kMaxPassBatch);
+    const bool dual = op == Q4RDNA_OP_SWIGLU;
     const long long warps =
-        (long long)d.sms * d.occ[variant()][batch_class(pb)] * kernel_cfg(variant(), pb).warps;
+        (long long)d.sms * d.occ[variant()][batch_class(pb)][dual] * kernel_cfg(variant(), pb, dual).warps;
     long long S = (warps + RB - 1) / RB;
     return make_split(G, (int)std::min<long long>(S, G)).S;
 }
@@ -613,16 +619,16 @@ q4rdna_status check_shape(int N, int K, int B) {
     return Q4RDNA_OK;
 }
 
-int grid_for(long long items, int pb, const DeviceInfo &d) {
-    const KernelCfg k = kernel_cfg(variant(), pb);
+int grid_for(long long items, int pb, bool dual, const DeviceInfo &d) {
+    const KernelCfg k = kernel_cfg(variant(), pb, dual);
     const long long want = (items + k.warps - 1) / k.warps;
-    const long long cap = (long long)d.sms * d.occ[variant()][batch_class(pb)];
+    const long long cap = (long long)d.sms * d.occ[variant()][batch_class(pb)][dual];
     return (int)std::max<long long>(1, std::min(want, cap));
 }
 
 // pb: batch columns of this pass (1..4).
-q4rdna_status launch(const Launch &L, int grid, int pb, cudaStream_t stream) {
-    const KernelCfg k = kernel_cfg(variant(), pb);
+q4rdna_status launch(const Launch &L, int grid, int pb, bool dual, cudaStream_t stream) {
+    const KernelCfg k = kernel_cfg(variant(), pb, dual);
     Launch arg = L;
     void *args[] = {&arg};
     if (cudaLaunchKernel(k.fn, dim3(grid), dim3(k.threads), args, (size_t)k.smem, stream) != cudaSuccess)
@@ -675,7 +681,8 @@ q4rdna_status gemv_common(int op, const uint8_t *w, const uint8_t *w2, const flo
         T.N = N; T.K = K; T.G = G; T.RB = RB; T.S = sp.S; T.Gs = sp.Gs; T.op = op; T.pad = 0;
         T.item_begin = 0;
         L.total_items = (long long)RB * sp.S;
-        st = launch(L, grid_for(L.total_items, pb, d), pb, stream);
+        const bool dual = op == Q4RDNA_OP_SWIGLU;
+        st = launch(L, grid_for(L.total_items, pb, dual, d), pb, dual, stream);
         if (st != Q4RDNA_OK) return st;
     }
     return Q4RDNA_OK;
@@ -688,6 +695,7 @@ using namespace q4;
 struct q4rdna_plan {
     int device = -1;
     int count = 0, B = 1, nb = 1, grid = 1;
+    bool dual = false;  // the plan holds a SwiGLU task
     long long items = 0;
     Task *table = nullptr;     // device
     void *workspace = nullptr; // device
@@ -832,8 +840,10 @@ q4rdna_status q4rdna_plan_create(const q4rdna_gemv_desc *descs, int count, int B
         q4rdna_plan_destroy(p);
         return Q4RDNA_ERR_CUDA;
     }
-    p->count = count; p->B = B; p->nb = B; p->items = items;
-    p->grid = grid_for(items, B, d);
+    bool any_dual = false;
+    for (int i = 0; i < count; ++i) any_dual = any_dual || descs[i].op == Q4RDNA_OP_SWIGLU;
+    p->count = count; p->B = B; p->nb = B; p->items = items; p->dual = any_dual;
+    p->grid = grid_for(items, B, any_dual, d);
     p->ws_bytes = ws_total; p->weight_bytes = wbytes; p->algo_bytes = abytes;
     *out = p;
     return Q4RDNA_OK;
@@ -848,7 +858,7 @@ q4rdna_status q4rdna_plan_run(q4rdna_plan *plan, q4rdna_stream_t stream) {
     L.ntasks = plan->count;
     L.B = plan->B;
     L.total_items = plan->items;
-    return launch(L, plan->grid, plan->nb, (cudaStream_t)stream);
+    return launch(L, plan->grid, plan->nb, plan->dual, (cudaStream_t)stream);
 }
 
 q4rdna_status q4rdna_plan_get_info(const q4rdna_plan *plan, q4rdna_plan_info *info) {

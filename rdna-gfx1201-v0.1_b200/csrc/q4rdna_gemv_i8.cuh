@@ -29,8 +29,9 @@
 // ascending order as sum = fma(scale * 2^e / 16, hi_limbs + lo_limbs, sum);
 // splits in ascending order in f32 (finish_rows).
 
+// One group of the activation, ready for the B operand.
 template <int BB>
-struct __align__(16) I8Smem {
+struct __align__(16) I8X {
     uint32_t xq[BB][Q4_GROUP];  // per k: L0 | L1 << 8 | L2 << 16 (s8 bytes)
     float up[BB];               // 2^e: undoes the group's power-of-two scaling
 };
@@ -47,15 +48,15 @@ __device__ __forceinline__ uint32_t limbs_of(float xs) {
     return ((uint32_t)L0 & 0xffu) | (((uint32_t)L1 & 0xffu) << 8) | (((uint32_t)L2 & 0xffu) << 16);
 }
 
+// Branch-free, so that the compiler can interleave it with the previous
+// group's MMAs (see run_item_i8).
 __device__ __forceinline__ void prep_group_i8(float2 v, uint32_t *xq_row, float *up, int lane) {
     const float m = warp_max(fmaxf(fabsf(v.x), fabsf(v.y)));
-    float f = 1.0f, u = 1.0f;
-    if (m > 0.0f) {
-        // biased exponent E of the max: scale by 2^(148 - E) so max*scale < 2^22
-        const uint32_t e = max((__float_as_uint(m) >> 23) & 0xffu, 40u);
-        f = __uint_as_float((275u - e) << 23);
-        u = __uint_as_float((e - 21u) << 23);
-    }
+    // biased exponent E of the max: scale by 2^(148 - E) so max*scale < 2^22
+    const uint32_t e = max((__float_as_uint(m) >> 23) & 0xffu, 40u);
+    const bool nz = m > 0.0f;
+    const float f = nz ? __uint_as_float((275u - e) << 23) : 1.0f;
+    const float u = nz ? __uint_as_float((e - 21u) << 23) : 1.0f;
     uint2 w;
     w.x = limbs_of(v.x * f);
     w.y = limbs_of(v.y * f);
@@ -113,14 +114,45 @@ __device__ __forceinline__ void load_step_i8(StepBufI8 &b, const uint8_t *tile, 
     for (int q = 0; q < 4; ++q) b.s[q] = ld_stream2(sp + 8 * q);
 }
 
-// One group of one tensor.  `next` is the tile of the step that follows (this
-// item's next step, the next item's first step, or this tile again at the very
-// end); slot m of `buf` is refilled from it as soon as it is consumed, so one
-// step of loads is always in flight and the loop has no branches.
-template <int BB>
-__device__ __forceinline__ void compute_step_i8(StepBufI8 &buf, const uint8_t *next, int c, int h,
-                                                const I8Smem<BB> &sm, float (&acc)[4][BB], int lane,
-                                                const I8Sel &sel) {
+// Where a step's code and scale words come from.  RegSource: the register
+// pipeline (slot m of the buffer is refilled from the following step's tile as
+// soon as it is consumed, so one step of loads is always in flight and the loop
+// has no branches).  SmemSource: a staged tile in shared memory.
+struct RegSource {
+    StepBufI8 &buf;
+    const uint8_t *nq, *ns;  // following step: code and scale addresses of this lane
+    __device__ __forceinline__ RegSource(StepBufI8 &b, const uint8_t *next, int c, int h)
+        : buf(b), nq(next + Q4_SCALE_BYTES + 32 * c + 16 * h), ns(next + 32 * h + 2 * c) {}
+    __device__ __forceinline__ void scales(uint32_t (&sw)[4]) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            sw[q] = buf.s[q];
+            buf.s[q] = ld_stream2(ns + 8 * q);
+        }
+    }
+    __device__ __forceinline__ uint4 codes(int m) {
+        const uint4 cur = buf.q[m];
+        buf.q[m] = ld_stream16(nq + 128 * m);
+        return cur;
+    }
+};
+
+struct SmemSource {
+    const uint8_t *q, *s;
+    __device__ __forceinline__ SmemSource(const uint8_t *tile, int c, int h)
+        : q(tile + Q4_SCALE_BYTES + 32 * c + 16 * h), s(tile + 32 * h + 2 * c) {}
+    __device__ __forceinline__ void scales(uint32_t (&sw)[4]) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) sw[k] = *reinterpret_cast<const unsigned short *>(s + 8 * k);
+    }
+    __device__ __forceinline__ uint4 codes(int m) { return *reinterpret_cast<const uint4 *>(q + 128 * m); }
+};
+
+// One group of one tensor: 16 (BB = 1) int8 MMAs per warp, exact int32 sums,
+// then the per-(row, group) scale in f32.
+template <int BB, class Src>
+__device__ __forceinline__ void mma_step_i8(Src &src, const I8X<BB> &sm, float (&acc)[4][BB], int lane,
+                                            const I8Sel &sel) {
     constexpr int NA = I8Shape<BB>::NA, NBP = I8Shape<BB>::NBP;
     int D[2][NA + NBP][4];
 #pragma unroll
@@ -130,19 +162,11 @@ __device__ __forceinline__ void compute_step_i8(StepBufI8 &buf, const uint8_t *n
 #pragma unroll
             for (int e = 0; e < 4; ++e) D[r][k][e] = 0;
     uint32_t sw[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) sw[q] = buf.s[q];
-    {
-        const uint8_t *sp = next + 32 * h + 2 * c;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) buf.s[q] = ld_stream2(sp + 8 * q);
-    }
-    const uint8_t *nq = next + Q4_SCALE_BYTES + 32 * c + 16 * h;
+    src.scales(sw);
     const int c4 = lane & 3;
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
-        const uint4 cur = buf.q[m];
-        buf.q[m] = ld_stream16(nq + 128 * m);
+        const uint4 cur = src.codes(m);
         uint32_t ba0[NA], ba1[NA], bb0[NBP], bb1[NBP];
         uint2 W[BB];
 #pragma unroll
@@ -244,10 +268,65 @@ __device__ __forceinline__ const uint8_t *item_tile0(const Task &T, int local, i
     return T.w + ((size_t)tile_row * T.G + g0) * Q4_TILE_BYTES;
 }
 
+// Flat cursor over the warp's activation groups (its items in order, each with
+// its groups): the raw f32 of the group it points at is fetched two groups
+// ahead of the group being multiplied.
+struct XCursor {
+    long long it;      // item (>= total: past the warp's last group)
+    int g, ng, g0, K;  // group within the item, the item's groups, first group, columns
+    const float *x;
+};
+
+__device__ __forceinline__ void xc_load(const Launch &L, XCursor &c) {
+    if (c.it >= L.total_items) return;
+    const Task &T = find_task(L, c.it);
+    const int local = (int)(c.it - T.item_begin);
+    c.g0 = (local % T.S) * T.Gs;
+    c.ng = min(T.Gs, T.G - c.g0);
+    c.g = 0;
+    c.K = T.K;
+    c.x = T.x;
+}
+
+__device__ __forceinline__ void xc_advance(const Launch &L, XCursor &c, long long nw) {
+    if (c.it >= L.total_items) return;
+    if (++c.g >= c.ng) {
+        c.it += nw;
+        xc_load(L, c);
+    }
+}
+
+template <int BB>
+__device__ __forceinline__ void xc_fetch(const Launch &L, const XCursor &c, int lane, float2 (&xv)[BB]) {
+    if (c.it >= L.total_items) return;
+#pragma unroll
+    for (int b = 0; b < BB; ++b)
+        if (b < L.B)
+            xv[b] = __ldg(reinterpret_cast<const float2 *>(c.x + (size_t)b * c.K + (size_t)(c.g0 + c.g) * Q4_GROUP) +
+                          lane);
+}
+
+// Per-warp state carried from item to item.
+template <int BB>
+struct I8Pipe {
+    StepBufI8 buf;   // code and scale words of the next step (register pipeline)
+    float2 xv[BB];   // raw x of the next group to prepare
+    XCursor xc;      // the group whose raw x is in xv
+    int par;         // activation buffer holding the group being multiplied
+};
+
+// Prepare the raw x in P.xv (the cursor's group) into activation buffer xs;
+// past the warp's last group it writes a spare buffer that is never read.
+template <int BB>
+__device__ __forceinline__ void prep_ahead(I8Pipe<BB> &P, I8X<BB> &xs, int lane) {
+#pragma unroll
+    for (int b = 0; b < BB; ++b) prep_group_i8(P.xv[b], xs.xq[b], &xs.up[b], lane);
+}
+
 template <int BB, bool DUAL>
-__device__ __forceinline__ void run_item_i8(const Task &T, int local, int B, I8Smem<BB> &sm, int lane,
-                                            const I8Sel &sel, StepBufI8 &buf, float2 (&xv)[BB], const Task *nT,
-                                            int nlocal) {
+__device__ __forceinline__ void run_item_i8(const Launch &L, const Task &T, int local, I8X<BB> (&xs)[2], int lane,
+                                            const I8Sel &sel, I8Pipe<BB> &P, const Task *nT, int nlocal,
+                                            long long nw) {
     const int rb = local / T.S, s = local % T.S;
     const int g0 = s * T.Gs, ng = min(T.Gs, T.G - g0);
     const int grp = lane >> 2, c = lane & 3, t = grp >> 1, h = grp & 1;
@@ -255,11 +334,10 @@ __device__ __forceinline__ void run_item_i8(const Task &T, int local, int B, I8S
     const bool valid = tile_row < (T.N >> 5);
     const uint8_t *base0 = item_tile0(T, local, lane, nullptr);
     const uint8_t *base1 = DUAL ? T.w2 + (base0 - T.w) : base0;
-    int ng0 = 0;
-    const uint8_t *after = nT ? item_tile0(*nT, nlocal, lane, &ng0) : nullptr;
+    const uint8_t *after = nT ? item_tile0(*nT, nlocal, lane, nullptr)
+                              : (DUAL ? base1 : base0) + (size_t)(ng - 1) * Q4_TILE_BYTES;
     const int nsteps = ng * (DUAL ? 2 : 1);
-    if (after == nullptr)  // last item of this warp: re-read its last tile (in bounds, never used)
-        after = (DUAL ? base1 : base0) + (size_t)(ng - 1) * Q4_TILE_BYTES;
+    (void)g0;
 
     float acc[2][4][BB];
 #pragma unroll
@@ -270,25 +348,7 @@ __device__ __forceinline__ void run_item_i8(const Task &T, int local, int B, I8S
             for (int b = 0; b < BB; ++b) acc[pl][q][b] = 0.0f;
 
     for (int st = 0; st < nsteps; ++st) {
-        const int tt = DUAL ? (st & 1) : 0, gl = DUAL ? (st >> 1) : st;
-        if (tt == 0) {
-            __syncwarp();
-#pragma unroll
-            for (int b = 0; b < BB; ++b)
-                if (b < B) prep_group_i8(xv[b], sm.xq[b], &sm.up[b], lane);
-            // next group's activation: this item's, or the next item's first group
-#pragma unroll
-            for (int b = 0; b < BB; ++b) {
-                if (b >= B) continue;
-                if (gl + 1 < ng)
-                    xv[b] = __ldg(reinterpret_cast<const float2 *>(T.x + (size_t)b * T.K +
-                                                                   (size_t)(g0 + gl + 1) * Q4_GROUP) + lane);
-                else if (nT)
-                    xv[b] = __ldg(reinterpret_cast<const float2 *>(nT->x + (size_t)b * nT->K +
-                                                                   (size_t)ng0 * Q4_GROUP) + lane);
-            }
-            __syncwarp();
-        }
+        const int tt = DUAL ? (st & 1) : 0;
         const uint8_t *next;
         if (st + 1 < nsteps) {
             const int tn = DUAL ? ((st + 1) & 1) : 0, gn = DUAL ? ((st + 1) >> 1) : st + 1;
@@ -296,17 +356,37 @@ __device__ __forceinline__ void run_item_i8(const Task &T, int local, int B, I8S
         } else {
             next = after;
         }
-        if (DUAL && tt)
-            compute_step_i8<BB>(buf, next, c, h, sm, acc[1], lane, sel);
-        else
-            compute_step_i8<BB>(buf, next, c, h, sm, acc[0], lane, sel);
+        RegSource src(P.buf, next, c, h);
+        I8X<BB> &cur = xs[P.par];
+        if (tt == 0) {
+            mma_step_i8<BB>(src, cur, acc[0], lane, sel);
+            // The next group's activation goes into the other buffer while the
+            // MMAs above drain: no branch in between, so the compiler can
+            // interleave the two independent chains.
+            prep_ahead<BB>(P, xs[P.par ^ 1], lane);
+        } else {
+            mma_step_i8<BB>(src, cur, acc[1], lane, sel);
+        }
+        if (!DUAL || tt == 1) {
+            // end of the group: the prepared buffer becomes current for everyone,
+            // and no lane still reads the old one when it is rewritten next
+            __syncwarp();
+            P.par ^= 1;
+            xc_advance(L, P.xc, nw);
+            xc_fetch<BB>(L, P.xc, lane, P.xv);
+        }
     }
-    finish_rows_i8<BB, DUAL>(T, rb, s, B, acc, lane, valid, tile_row, h, c);
+    if (DUAL)
+        finish_rows_i8<BB, true>(T, rb, s, L.B, acc, lane, valid, tile_row, h, c);
+    else
+        finish_rows_i8<BB, false>(T, rb, s, L.B, acc, lane, valid, tile_row, h, c);
 }
 
-template <int BB>
+// HAS_DUAL = false: the launch holds no SwiGLU task, so the SwiGLU path (and its
+// registers) is compiled out.
+template <int BB, bool HAS_DUAL>
 __global__ void __launch_bounds__(kThreads, BB <= 2 ? 2 : 1) q4_gemv_i8_kernel(const __grid_constant__ Launch L) {
-    __shared__ I8Smem<BB> smem[kWarps];
+    __shared__ I8X<BB> xsm[kWarps][2];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long nw = (long long)gridDim.x * kWarps;
     long long it = (long long)blockIdx.x * kWarps + warp;
@@ -319,26 +399,31 @@ __global__ void __launch_bounds__(kThreads, BB <= 2 ? 2 : 1) q4_gemv_i8_kernel(c
         sel.bcol_odd = n & 1;
     }
     const int c = lane & 3, h = (lane >> 2) & 1;
-    // Step 0 of the warp's first item and its first activation group.
-    StepBufI8 buf;
-    float2 xv[BB];
+    I8X<BB>(&xs)[2] = xsm[warp];
+    I8Pipe<BB> P;
+    P.par = 0;
     {
         const Task &T = find_task(L, it);
-        int g0 = 0;
-        load_step_i8(buf, item_tile0(T, (int)(it - T.item_begin), lane, &g0), c, h);
-#pragma unroll
-        for (int b = 0; b < BB; ++b)
-            xv[b] = b < L.B ? __ldg(reinterpret_cast<const float2 *>(T.x + (size_t)b * T.K + (size_t)g0 * Q4_GROUP) + lane)
-                            : make_float2(0.0f, 0.0f);
+        load_step_i8(P.buf, item_tile0(T, (int)(it - T.item_begin), lane, nullptr), c, h);
     }
+#pragma unroll
+    for (int b = 0; b < BB; ++b) P.xv[b] = make_float2(0.0f, 0.0f);
+    // the warp's first group into buffer 0, the second group's raw x in flight
+    P.xc.it = it;
+    xc_load(L, P.xc);
+    xc_fetch<BB>(L, P.xc, lane, P.xv);
+    prep_ahead<BB>(P, xs[0], lane);
+    xc_advance(L, P.xc, nw);
+    xc_fetch<BB>(L, P.xc, lane, P.xv);
+    __syncwarp();
     for (; it < L.total_items; it += nw) {
         const Task &T = find_task(L, it);
         const long long nit = it + nw;
         const Task *nT = nit < L.total_items ? &find_task(L, nit) : nullptr;
         const int nlocal = nT ? (int)(nit - nT->item_begin) : 0;
-        if (T.op == Q4RDNA_OP_SWIGLU)
-            run_item_i8<BB, true>(T, (int)(it - T.item_begin), L.B, smem[warp], lane, sel, buf, xv, nT, nlocal);
+        if (HAS_DUAL && T.op == Q4RDNA_OP_SWIGLU)
+            run_item_i8<BB, true>(L, T, (int)(it - T.item_begin), xs, lane, sel, P, nT, nlocal, nw);
         else
-            run_item_i8<BB, false>(T, (int)(it - T.item_begin), L.B, smem[warp], lane, sel, buf, xv, nT, nlocal);
+            run_item_i8<BB, false>(L, T, (int)(it - T.item_begin), xs, lane, sel, P, nT, nlocal, nw);
     }
 }
