@@ -180,36 +180,35 @@ def reference_cpu_rate(budget_s: float, threads: int):
 
 def build_step(model: str, rank: int, world: int, device, seed: int, layers: int = 0):
     """Weights (this rank's row shard of every tensor), activations and outputs
-    of one decode step, laid out so a step's inputs and outputs are each one
-    contiguous buffer (one copy each way for the end-to-end leg)."""
+    of one decode step, laid out by q4rdna.tp.Layout so that a step's inputs and
+    outputs are each one contiguous buffer (one copy each way for the
+    end-to-end leg, one all-gather for tensor parallelism)."""
     import torch
 
-    from q4rdna import synth
+    from q4rdna import synth, tp
 
     names = synth.model_tensors(model)
     if layers:
         names = [t for t in names if int(t[0].split(".")[1]) < layers]
-    shards = []
-    for (n, N, K) in names:
-        if N % (32 * world):
-            raise SystemExit(f"{n}: {N} rows do not shard into {world} x 32-row slices")
-        shards.append((n, N // world, K))
-    xsz = sum(K for _, _, K in shards)
-    ysz = sum(n for _, n, _ in shards)
-    x_all = torch.empty(xsz, dtype=torch.float32, device=device)
-    y_all = torch.empty(ysz, dtype=torch.float32, device=device)
+    try:
+        lay = tp.Layout(names, world, B=1)
+    except ValueError as e:
+        raise SystemExit(str(e))
+    x_all = torch.empty(lay.xsz, dtype=torch.float32, device=device)
+    y_all = torch.empty(lay.ysz, dtype=torch.float32, device=device)
     g = torch.Generator(device=device)
     g.manual_seed(seed)  # same activations on every rank (replicated x)
     x_all.normal_(generator=g)
-    descs, xo, yo = [], 0, 0
+    descs, xo = [], 0
     wbytes = abytes = 0
-    for i, (n, Ns, K) in enumerate(shards):
-        t = synth.tiles_torch(Ns, K, seed + 1 + i * world + rank, device)
-        descs.append({"tiles": t, "x": x_all[xo:xo + K].view(1, K), "y": y_all[yo:yo + Ns].view(1, Ns)})
-        xo += K
-        yo += Ns
-        wbytes += Ns * K * 34 // 64
-        abytes += Ns * K * 34 // 64 + 4 * K + 4 * Ns
+    for i, s in enumerate(lay.slots):
+        # each rank draws its own shard (same distributions; the shard of one
+        # full tensor is a byte slice, q4rdna.tp.shard_tiles)
+        t = synth.tiles_torch(s.rows, s.K, seed + 1 + i * world + rank, device)
+        descs.append({"tiles": t, "x": x_all[xo:xo + s.K].view(1, s.K), "y": lay.local_view(y_all, i)})
+        xo += s.K
+        wbytes += s.rows * s.K * 34 // 64
+        abytes += s.rows * s.K * 34 // 64 + 4 * s.K + 4 * s.rows
     return descs, x_all, y_all, wbytes, abytes, len(names)
 
 
@@ -218,6 +217,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     import q4rdna
+    from q4rdna import tp
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -242,7 +242,7 @@ def run_ours(args):
     def step():
         plan.run(stream)
         if world > 1:
-            dist.all_gather_into_tensor(gathered, y_all)
+            tp.all_gather(y_all, gathered)
 
     def barrier():
         torch.cuda.synchronize()
@@ -263,7 +263,7 @@ def run_ours(args):
             plan.run(stream)
             k_ev[i][1].record(stream)
             if world > 1:
-                dist.all_gather_into_tensor(gathered, y_all)
+                tp.all_gather(y_all, gathered)
         t1.record(stream)
         barrier()
     launches = q4rdna.launch_count() - l0
@@ -323,7 +323,7 @@ def run_ours(args):
             "e2e": {"value": round(total_algo / (e2e_ms / args.steps * 1e-3) / 1e9, 2), "unit": UNIT,
                     "us_per_step": round(e2e_ms / args.steps * 1e3, 2),
                     "h2d_bytes_per_step": x_all.numel() * 4, "d2h_bytes_per_step": y_host.numel() * 4},
-            "roofline": {"bound": "hbm", "kernel": "q4::q4_gemv_kernel<1> (plan)", "achieved": round(achieved, 1),
+            "roofline": {"bound": "hbm", "kernel": q4rdna.kernel_name() + " (plan)", "achieved": round(achieved, 1),
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "algo_bytes_per_launch": abytes, "kernel_us": round(kern_ms * 1e3, 2),
                          "traffic": ncu_traffic(f"{args.model}_tp{world}")},

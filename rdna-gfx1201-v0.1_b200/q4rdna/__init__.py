@@ -334,3 +334,13 @@ def registry_reset() -> None:
 
 def report_stats() -> None:
     _lib().q4rdna_report_stats()
+
+
+_KERNELS = {"i8": "q4::q4_gemv_i8_kernel", "i8tma": "q4::q4_gemv_i8_tma_kernel", "ldg": "q4::q4_gemv_kernel"}
+
+
+def kernel_name() -> str:
+    """Name of the GEMV kernel the library launches: the int8 tensor-core
+    kernel unless Q4RDNA_KERNEL selects another variant (read by the library
+    at its first launch with the same names)."""
+    return _KERNELS.get(os.environ.get("Q4RDNA_KERNEL") or "i8", _KERNELS["i8"])
