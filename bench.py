@@ -178,7 +178,7 @@ def reference_cpu_rate(budget_s: float, threads: int):
     return calls * nbytes / el / 1e9, kind, threads, sample
 
 
-def build_step(model: str, rank: int, world: int, device, seed: int, layers: int = 0):
+def build_step(model: str, rank: int, world: int, device, seed: int, layers: int = 0, B: int = 1):
     """Weights (this rank's row shard of every tensor), activations and outputs
     of one decode step, laid out by q4rdna.tp.Layout so that a step's inputs and
     outputs are each one contiguous buffer (one copy each way for the
@@ -191,11 +191,12 @@ def build_step(model: str, rank: int, world: int, device, seed: int, layers: int
     if layers:
         names = [t for t in names if int(t[0].split(".")[1]) < layers]
     try:
-        lay = tp.Layout(names, world, B=1)
+        lay = tp.Layout(names, world, B=B)
     except ValueError as e:
         raise SystemExit(str(e))
-    x_all = torch.empty(lay.xsz, dtype=torch.float32, device=device)
-    y_all = torch.empty(lay.ysz, dtype=torch.float32, device=device)
+    # tensor i: x block [B][K] at float B * (sum of earlier K), y block [B][rows]
+    x_all = torch.empty(B * lay.xsz, dtype=torch.float32, device=device)
+    y_all = torch.empty(B * lay.ysz, dtype=torch.float32, device=device)
     g = torch.Generator(device=device)
     g.manual_seed(seed)  # same activations on every rank (replicated x)
     x_all.normal_(generator=g)
@@ -205,11 +206,11 @@ def build_step(model: str, rank: int, world: int, device, seed: int, layers: int
         # each rank draws its own shard (same distributions; the shard of one
         # full tensor is a byte slice, q4rdna.tp.shard_tiles)
         t = synth.tiles_torch(s.rows, s.K, seed + 1 + i * world + rank, device)
-        descs.append({"tiles": t, "x": x_all[xo:xo + s.K].view(1, s.K), "y": lay.local_view(y_all, i)})
+        descs.append({"tiles": t, "x": x_all[B * xo:B * (xo + s.K)].view(B, s.K), "y": lay.local_view(y_all, i)})
         xo += s.K
         wbytes += s.rows * s.K * 34 // 64
-        abytes += s.rows * s.K * 34 // 64 + 4 * s.K + 4 * s.rows
-    return descs, x_all, y_all, wbytes, abytes, len(names)
+        abytes += s.rows * s.K * 34 // 64 + 4 * B * (s.K + s.rows)
+    return descs, x_all, y_all, wbytes, abytes, len(names), lay
 
 
 def run_ours(args):
@@ -233,16 +234,26 @@ def run_ours(args):
     if q4rdna.lib is None:
         raise SystemExit("libq4rdna.so not built")
 
-    descs, x_all, y_all, wbytes, abytes, ntensors = build_step(args.model, rank, world, dev, args.seed, args.layers)
-    plan = q4rdna.Plan(descs, B=1)
+    B = args.batch
+    descs, x_all, y_all, wbytes, abytes, ntensors, lay = build_step(args.model, rank, world, dev, args.seed,
+                                                                   args.layers, B)
+    plan = q4rdna.Plan(descs, B=B)
     info = plan.info()
     stream = torch.cuda.current_stream()
-    gathered = torch.empty(y_all.numel() * world, device=dev) if world > 1 else None
+    p2p = world > 1 and args.gather == "p2p"
+    gathered = torch.empty(y_all.numel() * world, device=dev) if world > 1 and not p2p else None
+    pg = tp.PeerGather(plan, lay, y_all) if p2p else None
+
+    def run_plan():
+        # p2p: the plan kernel stores into every rank's gathered buffer, then the flag exchange
+        return pg.run(stream) if p2p else plan.run(stream)
 
     def step():
-        plan.run(stream)
-        if world > 1:
+        out = run_plan()
+        if world > 1 and not p2p:
             tp.all_gather(y_all, gathered)
+            return gathered
+        return out if p2p else y_all
 
     def barrier():
         torch.cuda.synchronize()
@@ -260,9 +271,9 @@ def run_ours(args):
         t0.record(stream)
         for i in range(args.steps):
             k_ev[i][0].record(stream)
-            plan.run(stream)
+            run_plan()
             k_ev[i][1].record(stream)
-            if world > 1:
+            if world > 1 and not p2p:
                 tp.all_gather(y_all, gathered)
         t1.record(stream)
         barrier()
@@ -274,11 +285,10 @@ def run_ours(args):
     x_host = torch.empty(x_all.numel(), dtype=torch.float32, pin_memory=True)
     x_host.copy_(x_all)
     y_host = torch.empty(y_all.numel() * world, dtype=torch.float32, pin_memory=True)
-    out_dev = gathered if world > 1 else y_all
 
     def e2e_step():
         x_all.copy_(x_host, non_blocking=True)
-        step()
+        out_dev = step()
         y_host.copy_(out_dev, non_blocking=True)
 
     for _ in range(max(1, args.warmup)):
@@ -313,24 +323,30 @@ def run_ours(args):
             "us_per_step": round(step_ms * 1e3, 2), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int4 x f32 (fp16 scales, f32 accumulate)",
             "data": "synthetic: uniform int4 codes, fp16 scales |N(0,1)|*0.003, x ~ N(0,1) f32 (no Qwen3 weights offline)",
-            "config": {"workload": f"{args.model} decode-step weight stream: {ntensors} GEMVs batch 1"
+            "config": {"workload": f"{args.model} decode-step weight stream: {ntensors} GEMVs batch {B}"
                                    + (f" (first {args.layers} layers only)" if args.layers else "")
-                                   + (f", rows sharded over {world} GPUs + NCCL all-gather" if world > 1 else ""),
-                       "tensors": ntensors, "batch": 1, "weight_bytes_per_step": wbytes * world,
+                                   + (f", rows sharded over {world} GPUs + " + ("all-gather fused into the plan kernel (P2P stores)"
+                                      if p2p else "NCCL all-gather") if world > 1 else ""),
+                       "tensors": ntensors, "batch": B, "flops_per_step": 2 * B * wbytes * world * 64 // 34,
+                       "weight_bytes_per_step": wbytes * world,
                        "algo_bytes_per_step": total_algo, "parallelism": f"tp{world}" if world > 1 else "none",
                        "l2": f"no flush: {wbytes * world / 1e9:.2f} GB streamed per step >> 126 MB L2",
                        "plan_items": info["items"], "plan_grid": info["grid"]},
             "e2e": {"value": round(total_algo / (e2e_ms / args.steps * 1e-3) / 1e9, 2), "unit": UNIT,
                     "us_per_step": round(e2e_ms / args.steps * 1e3, 2),
                     "h2d_bytes_per_step": x_all.numel() * 4, "d2h_bytes_per_step": y_host.numel() * 4},
-            "roofline": {"bound": "hbm", "kernel": q4rdna.kernel_name() + " (plan)", "achieved": round(achieved, 1),
+            "roofline": {"bound": "hbm", "kernel": q4rdna.kernel_name(B) + (" (plan + fused gather)" if p2p else " (plan)"), "achieved": round(achieved, 1),
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "algo_bytes_per_launch": abytes, "kernel_us": round(kern_ms * 1e3, 2),
-                         "traffic": ncu_traffic(f"{args.model}_tp{world}")},
+                         "traffic": ncu_traffic(f"{args.model}_tp{world}" + (f"_b{B}" if B > 1 else ""))},
             "cpu_baseline": cpu,
             "gpu_launches": launches,
             "clocks": clk.summary(),
         }
+    if pg is not None:
+        torch.cuda.synchronize()
+        dist.barrier()
+        pg.close()
     plan.close()
     if world > 1:
         dist.barrier()
@@ -370,6 +386,10 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--ref-step-seconds", type=float, default=4.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gather", choices=["p2p", "nccl"], default="nccl",
+                    help="N > 1: all-gather fused into the plan kernel (p2p) or one NCCL all-gather per step")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="activation columns per GEMV (1..16; 5..16 run the tile path)")
     ap.add_argument("--layers", type=int, default=0,
                     help="only the first L layers (small cases for profiling); 0 = the whole model")
     args = ap.parse_args()

@@ -154,6 +154,38 @@ q4rdna_status q4rdna_plan_run(q4rdna_plan *plan, q4rdna_stream_t stream);
 q4rdna_status q4rdna_plan_get_info(const q4rdna_plan *plan, q4rdna_plan_info *info);
 void q4rdna_plan_destroy(q4rdna_plan *plan);
 
+/* ---- tensor parallelism: the all-gather fused into the plan kernel ----
+ * Replaces the NCCL all-gather of the row-sharded decode step (one process per
+ * GPU, each owning rows [r*N/P, (r+1)*N/P) of every tensor; the reference is
+ * single-GPU, so there is no reference counterpart).  The plan's outputs of a
+ * rank form one buffer of rank_floats floats starting at y_base (every
+ * descriptor's y lies inside it).  gathered0[p] / gathered1[p] are rank p's two
+ * gathered buffers of world * rank_floats floats (peer addresses mapped in this
+ * process with q4rdna_ipc_open, this rank's own at index rank); flags[p] is rank
+ * p's array of `world` u32 arrival flags, zero-initialised.  After this call,
+ * run n (1-based) of the plan stores every output also into slice `rank` of
+ * every rank's gathered buffer n % 2 (plain peer stores from the GEMV
+ * epilogue, no multicast), then raises its flag at every rank and waits, at
+ * most about 2 s, until every rank's run n has landed here.  On expiry bit 1 of
+ * q4rdna_take_fault is set.  Every rank must run the plan the same number of
+ * times.  world is 2..8. */
+q4rdna_status q4rdna_plan_set_gather(q4rdna_plan *plan, int world, int rank, const float *y_base,
+                                     size_t rank_floats, float *const *gathered0, float *const *gathered1,
+                                     uint32_t *const *flags);
+/* Gathered buffer (0 or 1) that the plan's last run filled; -1 before the first
+ * run or without a gather. */
+int q4rdna_plan_gather_parity(const q4rdna_plan *plan);
+
+/* Device memory shareable with the other processes of the box (cudaMalloc +
+ * CUDA IPC), zero-filled: the gathered buffers and flags above. */
+#define Q4RDNA_IPC_HANDLE_BYTES 64
+q4rdna_status q4rdna_ipc_alloc(size_t bytes, void **dev_ptr, unsigned char handle[Q4RDNA_IPC_HANDLE_BYTES]);
+q4rdna_status q4rdna_ipc_open(const unsigned char handle[Q4RDNA_IPC_HANDLE_BYTES], void **dev_ptr);
+/* Unmaps a q4rdna_ipc_open mapping. */
+q4rdna_status q4rdna_ipc_close(void *dev_ptr);
+/* Frees a q4rdna_ipc_alloc allocation (after every peer closed its mapping). */
+q4rdna_status q4rdna_ipc_free(void *dev_ptr);
+
 /* ---- sidecar (the reference's .q4rdna container, byte layout unchanged) ----
  * Header 48 B, entries 96 B, data at data_offset (source/q4rdna.cu:26-50).
  * Validation follows source/q4rdna.cu:131-152.  The whole data region is
@@ -195,6 +227,8 @@ uint64_t q4rdna_registry_hits(const char *weight_name);
 /* Device-side fault flags of the GEMV kernels since the last call, then cleared
  * (synchronises the device).  Bit 0: a pipeline wait ran past its iteration
  * limit (about 2 s), so the kernel stopped early and its outputs are invalid.
+ * Bit 1: a fused gather (q4rdna_plan_set_gather) stopped waiting for a peer's
+ * flag (about 2 s), so the gathered buffer of that run is incomplete.
  * 0 = no fault; 0xffffffff = the flag could not be read.  No reference
  * counterpart (the reference kernels never wait). */
 uint32_t q4rdna_take_fault(void);

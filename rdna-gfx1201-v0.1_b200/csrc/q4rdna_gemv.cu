@@ -55,6 +55,8 @@ namespace q4 {
 constexpr int kWarps = 8;             // warps per CTA
 constexpr int kThreads = kWarps * 32;
 
+constexpr int kMaxMirrors = 8;  // GPUs of one box
+
 struct Task {
     const uint8_t *w;   // primary tiles (W, or W_up for SwiGLU)
     const uint8_t *w2;  // W_gate for SwiGLU, else null
@@ -63,8 +65,10 @@ struct Task {
     float *y;           // [B][N]
     float *part;        // [S][planes][B][N] split partials (S > 1)
     unsigned *ticket;   // [RB] arrival counters (S > 1)
-    int N, K, G, RB, S, Gs, op, pad;
+    int N, K, G, RB, S, Gs, op;
+    int nmirror;        // tensor-parallel gather: copies of y in every rank's gathered buffer
     long long item_begin;
+    float *mirror[kMaxMirrors];  // [B][N] each, on this GPU or a peer (plain P2P stores)
 };
 
 struct Launch {
@@ -248,6 +252,13 @@ __device__ __forceinline__ void compute_step(StepBuf &buf, const uint8_t *next, 
     }
 }
 
+// Final store of one output: y, and its copies in the ranks' gathered buffers
+// when the launch gathers over peers (the fused all-gather).
+__device__ __forceinline__ void put_y(const Task &T, size_t idx, float v) {
+    T.y[idx] = v;
+    for (int p = 0; p < T.nmirror; ++p) T.mirror[p][idx] = v;
+}
+
 __device__ __forceinline__ float finish(float v, float gate, int op, const float *add, size_t idx) {
     if (op == Q4RDNA_OP_ADD) v += add[idx];
     if (op == Q4RDNA_OP_SWIGLU) v *= silu(gate);
@@ -273,7 +284,7 @@ __device__ __forceinline__ void reduce_splits(const Task &T, int rb, int B, int 
                 if (DUAL) s1 += __ldcg(p0 + sp * split_stride + (size_t)B * T.N);
             }
             const size_t idx = (size_t)b * T.N + row;
-            T.y[idx] = finish(s0, s1, T.op, T.add, idx);
+            put_y(T, idx, finish(s0, s1, T.op, T.add, idx));
         }
     }
     if (lane == 0) atomicExch(&T.ticket[rb], 0u);
@@ -299,7 +310,7 @@ __device__ __forceinline__ void finish_item(const Task &T, int rb, int s, int B,
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
                         const size_t idx = (size_t)b * T.N + row0 + 4 * j + e;
-                        T.y[idx] = finish(acc[0][j][nb][e], acc[DUAL ? 1 : 0][j][nb][e], T.op, T.add, idx);
+                        put_y(T, idx, finish(acc[0][j][nb][e], acc[DUAL ? 1 : 0][j][nb][e], T.op, T.add, idx));
                     }
                 }
         }
@@ -451,11 +462,12 @@ __global__ void q4_dequant_kernel(const uint8_t *tiles, float *W, int N, int K) 
 #include "q4rdna_gemv_tma.cuh"
 #include "q4rdna_gemv_i8.cuh"
 #include "q4rdna_gemv_i8_tma.cuh"
+#include "q4rdna_gemv_mb.cuh"
 
 // ------------------------------------------------------------------ host side
 
 constexpr int kMaxDevices = 64;
-constexpr int kMaxPassBatch = 4;  // batch columns per kernel pass (NB = 2)
+constexpr int kMaxPassBatch = 4;  // batch columns of the batch-1 kernels; above: the tile path
 std::atomic<uint64_t> g_launches{0};
 
 // Kernel variants: the int8 tensor-core kernel with register loads (default,
@@ -481,8 +493,19 @@ struct KernelCfg {
     int threads, smem, warps;
 };
 
-// Batch class of a kernel pass: 0 -> 1 column, 1 -> 2 columns, 2 -> 3..4 columns.
-int batch_class(int pb) { return pb <= 1 ? 0 : (pb == 2 ? 1 : 2); }
+// Batch class of a launch: 0 -> 1 column, 1 -> 2, 2 -> 3..4, 3 -> 5..8, 4 -> 9..16.
+constexpr int kBatchClasses = 5;
+int batch_class(int pb) { return pb <= 1 ? 0 : pb == 2 ? 1 : pb <= 4 ? 2 : pb <= 8 ? 3 : 4; }
+int class_batch(int bc) { return bc == 0 ? 1 : bc == 1 ? 2 : bc == 2 ? 4 : bc == 3 ? 8 : 16; }
+
+// Tile path for B = 5..16 (q4rdna_gemv_mb.cuh): one work item per CTA.
+KernelCfg mb_cfg(int pb, bool dual) {
+    if (pb <= 8)
+        return dual ? KernelCfg{(const void *)q4_gemv_mb_kernel<8, true>, kMbThreads, 0, 1}
+                    : KernelCfg{(const void *)q4_gemv_mb_kernel<8, false>, kMbThreads, 0, 1};
+    return dual ? KernelCfg{(const void *)q4_gemv_mb_kernel<16, true>, kMbThreads, 0, 1}
+                : KernelCfg{(const void *)q4_gemv_mb_kernel<16, false>, kMbThreads, 0, 1};
+}
 
 template <bool DUAL>
 KernelCfg i8_cfg(int pb) {
@@ -499,7 +522,21 @@ KernelCfg i8tma_cfg(int pb) {
 }
 
 // dual: the launch holds a SwiGLU task (kernels without the SwiGLU path need fewer registers).
+// Smallest batch that runs on the tile path.  Default 3: measured on the
+// Qwen3-8B step, the tile path takes B = 3..4 at a third of the batch-1 int8
+// kernel's time and ties it at B = 2.  Q4RDNA_TILE_MIN_BATCH (1, 2, 3 or 5)
+// overrides it for A/B measurements.
+int tile_min_batch() {
+    static const int v = [] {
+        const char *e = std::getenv("Q4RDNA_TILE_MIN_BATCH");
+        const int t = (e != nullptr && *e != '\0') ? std::atoi(e) : 3;
+        return std::max(1, std::min(t, kMaxPassBatch + 1));
+    }();
+    return v;
+}
+
 KernelCfg kernel_cfg(int v, int pb, bool dual = true) {
+    if (pb >= tile_min_batch()) return mb_cfg(pb, dual);
     switch (v) {
         case kI8Tma: return i8tma_cfg(pb);
         case kLdg:
@@ -511,7 +548,7 @@ KernelCfg kernel_cfg(int v, int pb, bool dual = true) {
 
 struct DeviceInfo {
     int sms = 0;
-    int occ[kVariants][3][2] = {};  // resident CTAs per SM: variant, batch class, SwiGLU (0: unknown)
+    int occ[kVariants][kBatchClasses][2] = {};  // resident CTAs per SM: variant, batch class, SwiGLU (0: unknown)
 };
 std::mutex g_dev_mutex;
 DeviceInfo g_dev[kMaxDevices];
@@ -527,10 +564,10 @@ bool device_info(DeviceInfo &out) {
         d.sms = sms;
     }
     const int v = variant();
-    for (int bc = 0; bc < 3; ++bc)
+    for (int bc = 0; bc < kBatchClasses; ++bc)
         for (int du = 0; du < 2; ++du) {
             if (d.occ[v][bc][du] != 0) continue;
-            const KernelCfg k = kernel_cfg(v, bc == 0 ? 1 : (bc == 1 ? 2 : 4), du != 0);
+            const KernelCfg k = kernel_cfg(v, class_batch(bc), du != 0);
             if (k.smem > 48 * 1024 &&
                 cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem) != cudaSuccess)
                 return false;
@@ -569,7 +606,7 @@ int select_split_for(int N, int K, int B, int op, const DeviceInfo &d) {
     (void)op;
     const int G = K / Q4_GROUP;
     const int RB = (N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
-    const int pb = std::min(B, kMaxPassBatch);
+    const int pb = B;
     const bool dual = op == Q4RDNA_OP_SWIGLU;
     const long long warps =
         (long long)d.sms * d.occ[variant()][batch_class(pb)][dual] * kernel_cfg(variant(), pb, dual).warps;
@@ -595,7 +632,7 @@ constexpr int kMaxSplitRows = (int)(kTicketArea / sizeof(unsigned)) * Q4_BLOCK_R
 
 size_t partial_bytes(int N, int B, int S, int op) {
     const int planes = op == Q4RDNA_OP_SWIGLU ? 2 : 1;
-    return (size_t)S * planes * std::min(B, kMaxPassBatch) * N * sizeof(float);
+    return (size_t)S * planes * B * N * sizeof(float);
 }
 
 // Workspace of one q4rdna_gemv* call: ticket area + partials (0 when S == 1).
@@ -626,7 +663,7 @@ int grid_for(long long items, int pb, bool dual, const DeviceInfo &d) {
     return (int)std::max<long long>(1, std::min(want, cap));
 }
 
-// pb: batch columns of this pass (1..4).
+// pb: batch columns of the launch (1..16).
 q4rdna_status launch(const Launch &L, int grid, int pb, bool dual, cudaStream_t stream) {
     const KernelCfg k = kernel_cfg(variant(), pb, dual);
     Launch arg = L;
@@ -662,35 +699,61 @@ q4rdna_status gemv_common(int op, const uint8_t *w, const uint8_t *w2, const flo
         ticket = static_cast<unsigned *>(ws);
         part = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + kTicketArea);
     }
-    // Batches above kMaxPassBatch run in passes of up to 4 columns; every pass
-    // re-streams the weights (the tensor-core tile path for B >= 8 replaces this).
-    for (int b0 = 0; b0 < B; b0 += kMaxPassBatch) {
-        const int pb = std::min(kMaxPassBatch, B - b0);
-        Launch L{};
-        L.table = nullptr;
-        L.ntasks = 1;
-        L.B = pb;
-        Task &T = L.one;
-        T.w = w;
-        T.w2 = w2;
-        T.x = x + (size_t)b0 * K;
-        T.add = add ? add + (size_t)b0 * N : nullptr;
-        T.y = y + (size_t)b0 * N;
-        T.part = part;
-        T.ticket = ticket;
-        T.N = N; T.K = K; T.G = G; T.RB = RB; T.S = sp.S; T.Gs = sp.Gs; T.op = op; T.pad = 0;
-        T.item_begin = 0;
-        L.total_items = (long long)RB * sp.S;
-        const bool dual = op == Q4RDNA_OP_SWIGLU;
-        st = launch(L, grid_for(L.total_items, pb, dual, d), pb, dual, stream);
-        if (st != Q4RDNA_OK) return st;
-    }
+    // One launch for the whole batch: B <= 4 on the batch-1 kernels, B = 5..16
+    // on the tile path; the weights are streamed once.
+    Launch L{};
+    L.table = nullptr;
+    L.ntasks = 1;
+    L.B = B;
+    Task &T = L.one;
+    T.w = w;
+    T.w2 = w2;
+    T.x = x;
+    T.add = add;
+    T.y = y;
+    T.part = part;
+    T.ticket = ticket;
+    T.N = N; T.K = K; T.G = G; T.RB = RB; T.S = sp.S; T.Gs = sp.Gs; T.op = op; T.nmirror = 0;
+    T.item_begin = 0;
+    L.total_items = (long long)RB * sp.S;
+    const bool dual = op == Q4RDNA_OP_SWIGLU;
+    st = launch(L, grid_for(L.total_items, B, dual, d), B, dual, stream);
+    if (st != Q4RDNA_OK) return st;
     return Q4RDNA_OK;
 }
 
 }  // namespace q4
 
 using namespace q4;
+
+// Flag exchange that closes a fused gather: after the plan kernel (stream
+// order), lane p raises this rank's flag at rank p, then waits, bounded, for
+// rank p's flag of this epoch here.
+struct GatherSignal {
+    uint32_t *peer[kMaxMirrors];  // every rank's flag array, as mapped in this process
+    uint32_t *local;              // this rank's flag array
+    int world, rank;
+    uint32_t epoch;
+};
+constexpr int kGatherTries = 1 << 22;  // x ~0.5 us sleep: about 2 s
+constexpr unsigned kFaultGatherTimeout = 2u;
+
+__global__ void q4_gather_signal_kernel(const __grid_constant__ GatherSignal a) {
+    const int p = threadIdx.x;
+    if (p >= a.world) return;
+    // the plan kernel's stores (peer ones included) precede this kernel in stream
+    // order; the system-scope fence orders them before the flag for the peers
+    __threadfence_system();
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.peer[p] + a.rank), "r"(a.epoch) : "memory");
+    int i = 0;
+    for (; i < kGatherTries; ++i) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a.local + p) : "memory");
+        if ((int)(v - a.epoch) >= 0) break;
+        __nanosleep(500);
+    }
+    if (i == kGatherTries) atomicOr(&g_fault, kFaultGatherTimeout);
+}
 
 struct q4rdna_plan {
     int device = -1;
@@ -701,6 +764,12 @@ struct q4rdna_plan {
     void *workspace = nullptr; // device
     size_t ws_bytes = 0;
     uint64_t weight_bytes = 0, algo_bytes = 0;
+    std::vector<Task> host;    // task table as uploaded (no gather)
+    // fused gather (q4rdna_plan_set_gather): one task table per gathered buffer
+    Task *gtable[2] = {nullptr, nullptr};
+    GatherSignal sig{};
+    uint32_t epoch = 0;
+    bool gather = false;
 };
 
 extern "C" {
@@ -780,7 +849,7 @@ q4rdna_status q4rdna_dequant_f32(const uint8_t *tiles, float *W, int N, int K, q
 q4rdna_status q4rdna_plan_create(const q4rdna_gemv_desc *descs, int count, int B, q4rdna_plan **out) {
     if (out == nullptr || descs == nullptr || count <= 0) return Q4RDNA_ERR_INVALID_ARGUMENT;
     *out = nullptr;
-    if (B < 1 || B > kMaxPassBatch) return Q4RDNA_ERR_UNSUPPORTED;
+    if (B < 1 || B > Q4RDNA_MAX_BATCH) return Q4RDNA_ERR_UNSUPPORTED;
     DeviceInfo d;
     if (!device_info(d)) return Q4RDNA_ERR_DEVICE;
     std::vector<Task> host(count);
@@ -802,18 +871,20 @@ q4rdna_status q4rdna_plan_create(const q4rdna_gemv_desc *descs, int count, int B
         const int planes = e.op == Q4RDNA_OP_SWIGLU ? 2 : 1;
         const int G = e.K / Q4_GROUP;
         const int RB = (e.N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
-        // Plans hold many tensors, so items are sized by bytes (~64 KB of tiles)
-        // instead of by occupancy: split overhead stays ~1% of the stream.
+        // Plans hold many tensors, so items are sized by bytes (~64 KB of tiles for
+        // the warp-item kernels, ~256 KB for the CTA-item tile path) instead of by
+        // occupancy: split overhead stays ~1% of the stream.
         int req = e.split;
         if (req <= 0) {
-            const int gs = std::max(1, 65536 / (Q4_BLOCK_TILES * Q4_TILE_BYTES * planes));
+            const int item_bytes = B >= tile_min_batch() ? 4 * 65536 : 65536;
+            const int gs = std::max(1, item_bytes / (Q4_BLOCK_TILES * Q4_TILE_BYTES * planes));
             req = (G + gs - 1) / gs;
         }
         const Split sp = make_split(G, req);
         Task &T = host[i];
         T.w = e.tiles; T.w2 = e.gate_tiles; T.x = e.x; T.add = e.add; T.y = e.y;
         T.part = nullptr; T.ticket = nullptr;
-        T.N = e.N; T.K = e.K; T.G = G; T.RB = RB; T.S = sp.S; T.Gs = sp.Gs; T.op = e.op; T.pad = 0;
+        T.N = e.N; T.K = e.K; T.G = G; T.RB = RB; T.S = sp.S; T.Gs = sp.Gs; T.op = e.op; T.nmirror = 0;
         T.item_begin = items;
         items += (long long)RB * sp.S;
         ws_off[i] = ws_total;
@@ -843,6 +914,7 @@ q4rdna_status q4rdna_plan_create(const q4rdna_gemv_desc *descs, int count, int B
     bool any_dual = false;
     for (int i = 0; i < count; ++i) any_dual = any_dual || descs[i].op == Q4RDNA_OP_SWIGLU;
     p->count = count; p->B = B; p->nb = B; p->items = items; p->dual = any_dual;
+    p->host = host;
     p->grid = grid_for(items, B, any_dual, d);
     p->ws_bytes = ws_total; p->weight_bytes = wbytes; p->algo_bytes = abytes;
     *out = p;
@@ -858,7 +930,107 @@ q4rdna_status q4rdna_plan_run(q4rdna_plan *plan, q4rdna_stream_t stream) {
     L.ntasks = plan->count;
     L.B = plan->B;
     L.total_items = plan->items;
-    return launch(L, plan->grid, plan->nb, plan->dual, (cudaStream_t)stream);
+    if (!plan->gather) return launch(L, plan->grid, plan->nb, plan->dual, (cudaStream_t)stream);
+    const uint32_t epoch = plan->epoch + 1;
+    L.table = plan->gtable[epoch & 1];
+    q4rdna_status st = launch(L, plan->grid, plan->nb, plan->dual, (cudaStream_t)stream);
+    if (st != Q4RDNA_OK) return st;
+    GatherSignal sg = plan->sig;
+    sg.epoch = epoch;
+    void *args[] = {&sg};
+    if (cudaLaunchKernel((const void *)q4_gather_signal_kernel, dim3(1), dim3(32), args, 0, (cudaStream_t)stream) !=
+        cudaSuccess)
+        return Q4RDNA_ERR_CUDA;
+    if (cudaGetLastError() != cudaSuccess) return Q4RDNA_ERR_CUDA;
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    plan->epoch = epoch;
+    return Q4RDNA_OK;
+}
+
+q4rdna_status q4rdna_plan_set_gather(q4rdna_plan *plan, int world, int rank, const float *y_base,
+                                     size_t rank_floats, float *const *gathered0, float *const *gathered1,
+                                     uint32_t *const *flags) {
+    if (plan == nullptr || y_base == nullptr || gathered0 == nullptr || gathered1 == nullptr || flags == nullptr)
+        return Q4RDNA_ERR_INVALID_ARGUMENT;
+    if (world < 2 || world > kMaxMirrors || rank < 0 || rank >= world || plan->gather)
+        return Q4RDNA_ERR_INVALID_ARGUMENT;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != plan->device) return Q4RDNA_ERR_DEVICE;
+    for (int p = 0; p < world; ++p)
+        if (gathered0[p] == nullptr || gathered1[p] == nullptr || flags[p] == nullptr ||
+            !aligned(gathered0[p], 4) || !aligned(gathered1[p], 4) || !aligned(flags[p], 4))
+            return Q4RDNA_ERR_INVALID_ARGUMENT;
+    // every output block [B][N] must lie inside this rank's slice
+    for (const Task &T : plan->host) {
+        if (T.y < y_base) return Q4RDNA_ERR_INVALID_ARGUMENT;
+        const size_t off = (size_t)(T.y - y_base);
+        if (off + (size_t)plan->B * T.N > rank_floats) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    }
+    for (int par = 0; par < 2; ++par) {
+        float *const *g = par == 0 ? gathered0 : gathered1;
+        std::vector<Task> t = plan->host;
+        for (Task &T : t) {
+            const size_t off = (size_t)(T.y - y_base);
+            T.nmirror = world;
+            for (int p = 0; p < world; ++p) T.mirror[p] = g[p] + (size_t)rank * rank_floats + off;
+        }
+        if (cudaMalloc(&plan->gtable[par], sizeof(Task) * t.size()) != cudaSuccess ||
+            cudaMemcpy(plan->gtable[par], t.data(), sizeof(Task) * t.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+            for (Task *&gt : plan->gtable) {
+                if (gt) cudaFree(gt);
+                gt = nullptr;
+            }
+            return Q4RDNA_ERR_CUDA;
+        }
+    }
+    GatherSignal &sg = plan->sig;
+    for (int p = 0; p < world; ++p) sg.peer[p] = flags[p];
+    sg.local = flags[rank];
+    sg.world = world;
+    sg.rank = rank;
+    plan->epoch = 0;
+    plan->gather = true;
+    return Q4RDNA_OK;
+}
+
+int q4rdna_plan_gather_parity(const q4rdna_plan *plan) {
+    if (plan == nullptr || !plan->gather || plan->epoch == 0) return -1;
+    return (int)(plan->epoch & 1u);
+}
+
+q4rdna_status q4rdna_ipc_alloc(size_t bytes, void **dev_ptr, unsigned char handle[Q4RDNA_IPC_HANDLE_BYTES]) {
+    if (bytes == 0 || dev_ptr == nullptr || handle == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    static_assert(sizeof(cudaIpcMemHandle_t) == Q4RDNA_IPC_HANDLE_BYTES, "IPC handle size");
+    void *p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return Q4RDNA_ERR_CUDA;
+    cudaIpcMemHandle_t h;
+    if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+        cudaFree(p);
+        return Q4RDNA_ERR_CUDA;
+    }
+    std::memcpy(handle, &h, sizeof(h));
+    *dev_ptr = p;
+    return Q4RDNA_OK;
+}
+
+q4rdna_status q4rdna_ipc_open(const unsigned char handle[Q4RDNA_IPC_HANDLE_BYTES], void **dev_ptr) {
+    if (handle == nullptr || dev_ptr == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void *p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return Q4RDNA_ERR_CUDA;
+    *dev_ptr = p;
+    return Q4RDNA_OK;
+}
+
+q4rdna_status q4rdna_ipc_close(void *dev_ptr) {
+    if (dev_ptr == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    return cudaIpcCloseMemHandle(dev_ptr) == cudaSuccess ? Q4RDNA_OK : Q4RDNA_ERR_CUDA;
+}
+
+q4rdna_status q4rdna_ipc_free(void *dev_ptr) {
+    if (dev_ptr == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    return cudaFree(dev_ptr) == cudaSuccess ? Q4RDNA_OK : Q4RDNA_ERR_CUDA;
 }
 
 q4rdna_status q4rdna_plan_get_info(const q4rdna_plan *plan, q4rdna_plan_info *info) {
@@ -876,6 +1048,8 @@ q4rdna_status q4rdna_plan_get_info(const q4rdna_plan *plan, q4rdna_plan_info *in
 void q4rdna_plan_destroy(q4rdna_plan *plan) {
     if (plan == nullptr) return;
     if (plan->table) cudaFree(plan->table);
+    for (Task *t : plan->gtable)
+        if (t) cudaFree(t);
     if (plan->workspace) cudaFree(plan->workspace);
     delete plan;
 }

@@ -26,7 +26,7 @@
 // of batch column 2p + bb.  So lane (grp, c) ends up holding, without any
 // shuffle, all three limb sums of rows 16h + c + {0, 4, 8, 12} of tile t.
 // Accumulation order: exact int32 inside a group; groups of a split in
-// ascending order as sum = fma(scale * 2^e / 16, hi_limbs + lo_limbs, sum);
+// ascending order as sum = fma(scale / 16, (hi_limbs + lo_limbs) * 2^e, sum);
 // splits in ascending order in f32 (finish_rows).
 
 // One group of the activation, ready for the B operand.
@@ -52,8 +52,10 @@ __device__ __forceinline__ uint32_t limbs_of(float xs) {
 // group's MMAs (see run_item_i8).
 __device__ __forceinline__ void prep_group_i8(float2 v, uint32_t *xq_row, float *up, int lane) {
     const float m = warp_max(fmaxf(fabsf(v.x), fabsf(v.y)));
-    // biased exponent E of the max: scale by 2^(148 - E) so max*scale < 2^22
-    const uint32_t e = max((__float_as_uint(m) >> 23) & 0xffu, 40u);
+    // biased exponent E of the max: scale by 2^(148 - E) so max*scale < 2^22.
+    // E >= 22 keeps both 2^(148 - E) and 2^(E - 148) normal f32 numbers; only
+    // groups whose largest |x| is below 2^-104 lose bits to the clamp.
+    const uint32_t e = max((__float_as_uint(m) >> 23) & 0xffu, 22u);
     const bool nz = m > 0.0f;
     const float f = nz ? __uint_as_float((275u - e) << 23) : 1.0f;
     const float u = nz ? __uint_as_float((e - 21u) << 23) : 1.0f;
@@ -63,6 +65,12 @@ __device__ __forceinline__ void prep_group_i8(float2 v, uint32_t *xq_row, float 
     reinterpret_cast<uint2 *>(xq_row)[lane] = w;
     if (lane == 0) *up = u;
 }
+
+// An int32 sum S with |S| < 2^22 accumulated on top of kMagicI reads, as f32
+// bits, 1.5 * 2^23 + S exactly: the int -> float conversion becomes one
+// subtraction (or one fma with a scaled bias) on the full-rate pipe.
+constexpr int kMagicI = 0x4B400000;
+constexpr float kMagicF = 12582912.0f;  // 1.5 * 2^23
 
 __device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                           uint32_t b0, uint32_t b1) {
@@ -160,7 +168,7 @@ __device__ __forceinline__ void mma_step_i8(Src &src, const I8X<BB> &sm, float (
 #pragma unroll
         for (int k = 0; k < NA + NBP; ++k)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) D[r][k][e] = 0;
+            for (int e = 0; e < 4; ++e) D[r][k][e] = kMagicI;  // read back as f32 with one add
     uint32_t sw[4];
     src.scales(sw);
     const int c4 = lane & 3;
@@ -208,10 +216,13 @@ __device__ __forceinline__ void mma_step_i8(Src &src, const I8X<BB> &sm, float (
         const float sc = __half2float(__ushort_as_half((unsigned short)sw[q])) * 0.0625f;
 #pragma unroll
         for (int b = 0; b < BB; ++b) {
-            const int l2 = D[r][b][2 * hf], l1 = D[r][b][2 * hf + 1];
-            const int l0 = D[r][NA + (b >> 1)][2 * hf + (b & 1)];
-            const float v = fmaf((float)l2, 65536.0f, (float)(l1 * 256 + l0));
-            acc[q][b] = fmaf(sc * sm.up[b], v, acc[q][b]);
+            // limb sums over kMagicI (|S| <= 64 * 128 * 128 < 2^22): L1 * 256 and
+            // L2 * 65536 come out of the fma exactly; v rounds once per add
+            const float l0 = __int_as_float(D[r][NA + (b >> 1)][2 * hf + (b & 1)]) - kMagicF;
+            const float lo = fmaf(__int_as_float(D[r][b][2 * hf + 1]), 256.0f, -256.0f * kMagicF) + l0;
+            const float v = fmaf(__int_as_float(D[r][b][2 * hf]), 65536.0f, -65536.0f * kMagicF) + lo;
+            // v * 2^e is exact (a power of two, in range), so this is one rounding
+            acc[q][b] = fmaf(sc, v * sm.up[b], acc[q][b]);
         }
     }
 }
@@ -229,7 +240,7 @@ __device__ __forceinline__ void finish_rows_i8(const Task &T, int rb, int s, int
                 for (int b = 0; b < BB; ++b) {
                     if (b >= B) continue;
                     const size_t idx = (size_t)b * T.N + row0 + 4 * q;
-                    T.y[idx] = finish(acc[0][q][b], acc[DUAL ? 1 : 0][q][b], T.op, T.add, idx);
+                    put_y(T, idx, finish(acc[0][q][b], acc[DUAL ? 1 : 0][q][b], T.op, T.add, idx));
                 }
         }
         return;

@@ -66,6 +66,12 @@ def _bind(lib):
         "q4rdna_plan_run": (c_int, [P, P]),
         "q4rdna_plan_get_info": (c_int, [P, POINTER(PlanInfo)]),
         "q4rdna_plan_destroy": (None, [P]),
+        "q4rdna_plan_set_gather": (c_int, [P, c_int, c_int, P, c_size_t, POINTER(P), POINTER(P), POINTER(P)]),
+        "q4rdna_plan_gather_parity": (c_int, [P]),
+        "q4rdna_ipc_alloc": (c_int, [c_size_t, POINTER(P), ctypes.c_char_p]),
+        "q4rdna_ipc_open": (c_int, [ctypes.c_char_p, POINTER(P)]),
+        "q4rdna_ipc_close": (c_int, [P]),
+        "q4rdna_ipc_free": (c_int, [P]),
         "q4rdna_sidecar_open": (c_int, [c_char_p, c_int, POINTER(P)]),
         "q4rdna_sidecar_close": (None, [P]),
         "q4rdna_sidecar_count": (c_int, [P]),
@@ -94,6 +100,8 @@ SYMBOLS = [
     "q4rdna_workspace_init", "q4rdna_gemv", "q4rdna_gemv_add", "q4rdna_gemv_swiglu", "q4rdna_dequant_f32",
     "q4rdna_gemv_noalloc",
     "q4rdna_plan_create", "q4rdna_plan_run", "q4rdna_plan_get_info", "q4rdna_plan_destroy",
+    "q4rdna_plan_set_gather", "q4rdna_plan_gather_parity", "q4rdna_ipc_alloc", "q4rdna_ipc_open",
+    "q4rdna_ipc_close", "q4rdna_ipc_free",
     "q4rdna_sidecar_open", "q4rdna_sidecar_close", "q4rdna_sidecar_count", "q4rdna_sidecar_entry",
     "q4rdna_sidecar_find", "q4rdna_mul_mat", "q4rdna_mul_mat_add", "q4rdna_mul_mat_glu",
     "q4rdna_launch_count", "q4rdna_take_fault", "q4rdna_registry_hits", "q4rdna_report_stats", "q4rdna_registry_reset",
@@ -339,8 +347,10 @@ def report_stats() -> None:
 _KERNELS = {"i8": "q4::q4_gemv_i8_kernel", "i8tma": "q4::q4_gemv_i8_tma_kernel", "ldg": "q4::q4_gemv_kernel"}
 
 
-def kernel_name() -> str:
-    """Name of the GEMV kernel the library launches: the int8 tensor-core
-    kernel unless Q4RDNA_KERNEL selects another variant (read by the library
-    at its first launch with the same names)."""
+def kernel_name(B: int = 1) -> str:
+    """Name of the GEMV kernel the library launches for batch B: the tile path
+    for B = 3..16, else the int8 tensor-core kernel unless Q4RDNA_KERNEL selects
+    another variant (read by the library at its first launch, same names)."""
+    if B >= int(os.environ.get("Q4RDNA_TILE_MIN_BATCH") or 3):
+        return "q4::q4_gemv_mb_kernel"
     return _KERNELS.get(os.environ.get("Q4RDNA_KERNEL") or "i8", _KERNELS["i8"])

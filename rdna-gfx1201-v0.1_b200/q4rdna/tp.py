@@ -119,3 +119,89 @@ def all_gather(y_rank, gathered, group=None) -> None:
     world = dist.get_world_size(group)
     parts = list(gathered.view(world, -1).unbind(0))
     dist.all_gather(parts, y_rank.reshape(-1), group=group)
+
+
+class _DeviceBuffer:
+    """Exposes library-owned device memory to torch (no copy)."""
+
+    def __init__(self, ptr: int, nfloats: int):
+        self.__cuda_array_interface__ = {"shape": (nfloats,), "typestr": "<f4", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerGather:
+    """The all-gather fused into the plan kernel (q4rdna_plan_set_gather).
+
+    Every rank allocates two gathered buffers (world x its y buffer) and one
+    flag array in IPC-shareable device memory, exchanges the handles over the
+    process group and maps its peers' buffers.  Each plan run then stores every
+    output also into this rank's slice of every rank's gathered buffer (plain
+    NVLink peer stores from the GEMV epilogue) and ends with a bounded flag
+    exchange, so that when the run's work on this GPU has finished, the
+    gathered buffer it returns holds every rank's outputs of that run.  Runs
+    alternate between the two buffers, so a rank running one step ahead never
+    overwrites a buffer a slower rank is still reading.
+    """
+
+    def __init__(self, plan, layout: Layout, y_rank, group=None):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _lib, check
+
+        lib = _lib()
+        self._lib = lib
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        if y_rank.numel() != layout.B * layout.ysz:
+            raise ValueError("y buffer does not match the layout")
+        self.world, self.rank, self.plan = world, rank, plan
+        nrank = layout.B * layout.ysz
+        sizes = [4 * world * nrank, 4 * world * nrank, 256]
+        self._own, handles = [], []
+        for nb in sizes:
+            ptr, h = ctypes.c_void_p(), ctypes.create_string_buffer(64)
+            check(lib.q4rdna_ipc_alloc(nb, ctypes.byref(ptr), h), "ipc_alloc")
+            self._own.append(ptr.value)
+            handles.append(h.raw)
+        allh = [None] * world
+        dist.all_gather_object(allh, handles, group=group)
+        self._opened = []
+        maps = [[0] * world for _ in sizes]
+        for p in range(world):
+            for k in range(len(sizes)):
+                if p == rank:
+                    maps[k][p] = self._own[k]
+                    continue
+                ptr = ctypes.c_void_p()
+                check(lib.q4rdna_ipc_open(allh[p][k], ctypes.byref(ptr)), "ipc_open")
+                self._opened.append(ptr.value)
+                maps[k][p] = ptr.value
+        arr = [(ctypes.c_void_p * world)(*m) for m in maps]
+        check(lib.q4rdna_plan_set_gather(plan._h, world, rank, y_rank.data_ptr(), nrank, arr[0], arr[1], arr[2]),
+              "plan_set_gather")
+        dev = y_rank.device
+        self.gathered = [torch.as_tensor(_DeviceBuffer(self._own[k], world * nrank), device=dev) for k in (0, 1)]
+        # every rank has mapped every buffer before any rank's first run
+        dist.barrier(group=group)
+
+    def run(self, stream=None):
+        """One plan run with its fused gather; returns the gathered buffer
+        ([world * B * ysz] f32, rank-major) that the run fills."""
+        self.plan.run(stream)
+        return self.gathered[self._lib.q4rdna_plan_gather_parity(self.plan._h)]
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's.  Every rank must have
+        finished its runs (the caller synchronises and barriers first)."""
+        import torch.distributed as dist
+
+        for p in self._opened:
+            self._lib.q4rdna_ipc_close(p)
+        self._opened = []
+        self.gathered = []
+        dist.barrier()  # peers have unmapped this rank's buffers
+        for p in self._own:
+            self._lib.q4rdna_ipc_free(p)
+        self._own = []

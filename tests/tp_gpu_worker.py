@@ -71,6 +71,20 @@ def main() -> int:
             if not np.array_equal(y[:, r0:r0 + rows].view(np.uint32), lay.local_view(own, i).view(np.uint32)):
                 print(f"rank {rank} B={B} {n}: own slice changed by the gather", flush=True)
                 bad += 1
+        # the fused gather: the same plan stores into every rank's gathered
+        # buffer itself; both buffers (two runs) must equal the NCCL gather bit for bit
+        want = gathered.cpu().numpy().view(np.uint32).copy()
+        pg = tp.PeerGather(plan, lay, y_all)
+        for run in range(3):
+            for d, (tiles, x) in zip(descs, host):
+                d["x"].copy_(torch.from_numpy(x))
+            got = pg.run()
+            torch.cuda.synchronize()
+            if not np.array_equal(got.cpu().numpy().view(np.uint32), want):
+                print(f"rank {rank} B={B} run {run}: fused gather differs from the NCCL gather", flush=True)
+                bad += 1
+        dist.barrier()
+        pg.close()
         plan.close()
         fault = q4rdna.take_fault()
         if fault:
