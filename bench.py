@@ -386,18 +386,23 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--ref-step-seconds", type=float, default=4.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--gather", choices=["p2p", "nccl"], default="nccl",
+    ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
                     help="N > 1: all-gather fused into the plan kernel (p2p) or one NCCL all-gather per step")
     ap.add_argument("--batch", type=int, default=1,
-                    help="activation columns per GEMV (1..16; 5..16 run the tile path)")
+                    help="activation columns per GEMV (1..16; 3..16 run the tile path)")
     ap.add_argument("--layers", type=int, default=0,
                     help="only the first L layers (small cases for profiling); 0 = the whole model")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    # stdout carries exactly one JSON line: library chatter (the NCCL version
+    # banner, warnings) goes to stderr for the whole run
+    sys.stdout.flush()
+    result = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     out = run_reference(args) if args.impl == "reference" else run_ours(args)
     if out is not None:
-        print(json.dumps(out), flush=True)
+        print(json.dumps(out), file=result, flush=True)
 
 
 if __name__ == "__main__":
