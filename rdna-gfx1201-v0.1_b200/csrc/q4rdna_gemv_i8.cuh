@@ -8,11 +8,13 @@
 //     weights, no conversion and no offset to undo;
 //   * activation: per group, x is scaled by a power of two so its largest
 //     magnitude lies in [2^21, 2^22), rounded to an integer X (error <= 2^-22 of
-//     the group's largest |x|) and split exactly into three signed 8-bit limbs,
-//     X = L2 * 65536 + L1 * 256 + L0;
-//   * mma.sync m16n8k32 s8 x s8 -> s32 sums the products of one group exactly;
-//     the epilogue combines the limbs in f32 and applies scale * 2^e / 16 once
-//     per (row, group), as the reference applies its scale (q4rdna.cu:370-371).
+//     the group's largest |x|) and used as its own bytes,
+//     X = B2 * 65536 + B1 * 256 + B0 with B0, B1 unsigned and B2 = X >> 16
+//     signed: no limb arithmetic;
+//   * mma.sync m16n8k32 s8 x u8 (bytes 0, 1) and s8 x s8 (byte 2) -> s32 sum
+//     the products of one group exactly; the epilogue combines the byte sums in
+//     f32 and applies scale * 2^e / 16 once per (row, group), as the reference
+//     applies its scale (q4rdna.cu:370-371).
 //
 // Fragment mapping (m16n8k32, A row-major, B col-major).  Lane (grp, c) loads,
 // for k-step m, 16 bytes of tile t = grp >> 1 at 64 + 128m + 32c + 16h
@@ -20,11 +22,11 @@
 // i = 4m + c.  Row set r (r = 0, 1) uses q[2r] for MMA row grp and q[2r+1] for
 // MMA row grp + 8: A k-slots 4c + j hold the low-nibble column 2i of row
 // (16h + 8r + j [+4]), k-slots 16 + 4c + j the high-nibble column 2i + 1.  The
-// four rows of a register are separated by the B operand: for "MMA a" column
-// n = 2 * slot + limb carries limb L2 (limb 0) or L1 (limb 1) of x placed in
-// byte `slot` of the B register; for "MMA b" column 2 * slot + bb carries L0
-// of batch column 2p + bb.  So lane (grp, c) ends up holding, without any
-// shuffle, all three limb sums of rows 16h + c + {0, 4, 8, 12} of tile t.
+// four rows of a register are separated by the B operand: for "MMA a" (u8)
+// column n = 2 * slot + q carries byte B1 (q = 0) or B0 (q = 1) of X placed in
+// byte `slot` of the B register; for "MMA b" (s8) column 2 * slot + bb carries
+// B2 of batch column 2p + bb.  So lane (grp, c) ends up holding, without any
+// shuffle, all three byte sums of rows 16h + c + {0, 4, 8, 12} of tile t.
 // Accumulation order: exact int32 inside a group; groups of a split in
 // ascending order as sum = fma(scale / 16, (hi_limbs + lo_limbs) * 2^e, sum);
 // splits in ascending order in f32 (finish_rows).
@@ -32,21 +34,9 @@
 // One group of the activation, ready for the B operand.
 template <int BB>
 struct __align__(16) I8X {
-    uint32_t xq[BB][Q4_GROUP];  // per k: L0 | L1 << 8 | L2 << 16 (s8 bytes)
+    uint32_t xq[BB][Q4_GROUP];  // per k: the integer X (bytes B0, B1, B2 used)
     float up[BB];               // 2^e: undoes the group's power-of-two scaling
 };
-
-// Signed byte 0 of v, sign-extended to 32 bits.
-__device__ __forceinline__ int sext8(int v) { return (int)(int8_t)(v & 0xff); }
-
-__device__ __forceinline__ uint32_t limbs_of(float xs) {
-    const int X = __float2int_rn(xs);
-    const int L0 = sext8(X);
-    const int X1 = (X - L0) >> 8;
-    const int L1 = sext8(X1);
-    const int L2 = (X1 - L1) >> 8;  // |X| <= 2^22 -> L2 in [-64, 64]
-    return ((uint32_t)L0 & 0xffu) | (((uint32_t)L1 & 0xffu) << 8) | (((uint32_t)L2 & 0xffu) << 16);
-}
 
 // Branch-free, so that the compiler can interleave it with the previous
 // group's MMAs (see run_item_i8).
@@ -60,8 +50,8 @@ __device__ __forceinline__ void prep_group_i8(float2 v, uint32_t *xq_row, float 
     const float f = nz ? __uint_as_float((275u - e) << 23) : 1.0f;
     const float u = nz ? __uint_as_float((e - 21u) << 23) : 1.0f;
     uint2 w;
-    w.x = limbs_of(v.x * f);
-    w.y = limbs_of(v.y * f);
+    w.x = (uint32_t)__float2int_rn(v.x * f);  // |X| < 2^22: byte 2 as s8 is X >> 16
+    w.y = (uint32_t)__float2int_rn(v.y * f);
     reinterpret_cast<uint2 *>(xq_row)[lane] = w;
     if (lane == 0) *up = u;
 }
@@ -80,18 +70,27 @@ __device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1,
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Number of "MMA b" instructions (L0 of two batch columns each) for BB columns.
+// Same with unsigned B bytes.
+__device__ __forceinline__ void imma16832_u(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                            uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Number of "MMA a" and "MMA b" instructions (B2 of two batch columns each) for BB columns.
 template <int BB>
 struct I8Shape {
-    static constexpr int NA = BB;             // "MMA a": L2, L1 of one batch column
-    static constexpr int NBP = (BB + 1) / 2;  // "MMA b": L0 of a batch pair
+    static constexpr int NA = BB;             // "MMA a": B1, B0 of one batch column
+    static constexpr int NBP = (BB + 1) / 2;  // "MMA b": B2 of a batch pair
 };
 
 // B-operand selectors of this lane (fixed per kernel): byte `slot` of the
-// register takes limb byte `src` of the per-k word; all other bytes are zero.
+// register takes byte `src` of the per-k word X; all other bytes are zero.
 struct I8Sel {
-    uint32_t a;      // MMA a: src 2 (L2) or 1 (L1)
-    uint32_t b;      // MMA b: src 0 (L0), or all-zero when the batch is absent
+    uint32_t a;      // MMA a: src 1 (B1) or 0 (B0)
+    uint32_t b;      // MMA b: src 2 (B2), or all-zero when the batch is absent
     int bcol_odd;    // MMA b: this lane's column carries batch 2p + 1
 };
 
@@ -203,24 +202,25 @@ __device__ __forceinline__ void mma_step_i8(Src &src, const I8X<BB> &sm, float (
             const uint32_t a2 = wa & 0xF0F0F0F0u;         // 16 * high-nibble code (column 2i + 1)
             const uint32_t a3 = wb & 0xF0F0F0F0u;
 #pragma unroll
-            for (int b = 0; b < NA; ++b) imma16832(D[r][b], a0, a1, a2, a3, ba0[b], ba1[b]);
+            for (int b = 0; b < NA; ++b) imma16832_u(D[r][b], a0, a1, a2, a3, ba0[b], ba1[b]);
 #pragma unroll
             for (int p = 0; p < NBP; ++p) imma16832(D[r][NA + p], a0, a1, a2, a3, bb0[p], bb1[p]);
         }
     }
-    // rows 16h + c + 4q, q = 2r + half: limb sums L2 = Da[2*half], L1 = Da[2*half+1],
-    // L0 = Db[2*half + (b & 1)]
+    // rows 16h + c + 4q, q = 2r + half: byte sums S1 = Da[2*half], S0 = Da[2*half+1],
+    // S2 = Db[2*half + (b & 1)]
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
         const int r = q >> 1, hf = q & 1;
         const float sc = __half2float(__ushort_as_half((unsigned short)sw[q])) * 0.0625f;
 #pragma unroll
         for (int b = 0; b < BB; ++b) {
-            // limb sums over kMagicI (|S| <= 64 * 128 * 128 < 2^22): L1 * 256 and
-            // L2 * 65536 come out of the fma exactly; v rounds once per add
-            const float l0 = __int_as_float(D[r][NA + (b >> 1)][2 * hf + (b & 1)]) - kMagicF;
-            const float lo = fmaf(__int_as_float(D[r][b][2 * hf + 1]), 256.0f, -256.0f * kMagicF) + l0;
-            const float v = fmaf(__int_as_float(D[r][b][2 * hf]), 65536.0f, -65536.0f * kMagicF) + lo;
+            // byte sums over kMagicI (|S| <= 64 * 128 * 255 < 2^22): S1 * 256 and
+            // S2 * 65536 come out of the fma exactly; v rounds once per add
+            const float s0 = __int_as_float(D[r][b][2 * hf + 1]) - kMagicF;
+            const float lo = fmaf(__int_as_float(D[r][b][2 * hf]), 256.0f, -256.0f * kMagicF) + s0;
+            const float v =
+                fmaf(__int_as_float(D[r][NA + (b >> 1)][2 * hf + (b & 1)]), 65536.0f, -65536.0f * kMagicF) + lo;
             // v * 2^e is exact (a power of two, in range), so this is one rounding
             acc[q][b] = fmaf(sc, v * sm.up[b], acc[q][b]);
         }
@@ -405,8 +405,8 @@ __global__ void __launch_bounds__(kThreads, BB <= 2 ? 2 : 1) q4_gemv_i8_kernel(c
     I8Sel sel;
     {
         const int n = lane >> 2;  // this lane's B column
-        sel.a = sel_one(n >> 1, (n & 1) ? 1 : 2);
-        sel.b = sel_one(n >> 1, 0);
+        sel.a = sel_one(n >> 1, (n & 1) ? 0 : 1);
+        sel.b = sel_one(n >> 1, 2);
         sel.bcol_odd = n & 1;
     }
     const int c = lane & 3, h = (lane >> 2) & 1;

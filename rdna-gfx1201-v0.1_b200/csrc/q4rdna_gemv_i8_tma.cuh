@@ -86,8 +86,8 @@ __global__ void __launch_bounds__(R::THREADS, R::MINB) q4_gemv_i8_tma_kernel(con
     I8Sel sel;
     {
         const int n = lane >> 2;  // this lane's B column
-        sel.a = sel_one(n >> 1, (n & 1) ? 1 : 2);
-        sel.b = sel_one(n >> 1, 0);
+        sel.a = sel_one(n >> 1, (n & 1) ? 0 : 1);
+        sel.b = sel_one(n >> 1, 2);
         sel.bcol_odd = n & 1;
     }
     const int grp = lane >> 2, c = lane & 3, t = grp >> 1, h = grp & 1;
