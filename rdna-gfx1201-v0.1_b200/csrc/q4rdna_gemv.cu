@@ -755,6 +755,8 @@ __global__ void q4_gather_signal_kernel(const __grid_constant__ GatherSignal a) 
     if (i == kGatherTries) atomicOr(&g_fault, kFaultGatherTimeout);
 }
 
+constexpr int kDefaultSegments = 16;  // plan runs (measured on the Qwen3-8B step: 8..16 best)
+
 struct q4rdna_plan {
     int device = -1;
     int count = 0, B = 1, nb = 1, grid = 1;
@@ -765,12 +767,35 @@ struct q4rdna_plan {
     size_t ws_bytes = 0;
     uint64_t weight_bytes = 0, algo_bytes = 0;
     std::vector<Task> host;    // task table as uploaded (no gather)
+    // q4rdna_plan_run_host: consecutive task ranges with their own device tables
+    struct Segment {
+        int first = 0, count = 0;
+        long long items = 0;
+        int grid = 1;
+        Task *table = nullptr;  // item_begin rebased to the segment
+        size_t x_lo = 0, x_hi = 0, y_lo = 0, y_hi = 0;  // byte ranges from x_dev / y_dev
+        cudaEvent_t x_ready = nullptr, y_ready = nullptr;
+    };
+    std::vector<Segment> segs;
+    int seg_request = -1;
+    int run_segments = kDefaultSegments;  // q4rdna_plan_run: 1 = one launch
+    const void *seg_x = nullptr, *seg_y = nullptr;
+    cudaStream_t h2d = nullptr, d2h = nullptr;
+    cudaStream_t comp[2] = {nullptr, nullptr};  // segments alternate, so one's tail overlaps the next
+    cudaEvent_t start = nullptr, done = nullptr;
     // fused gather (q4rdna_plan_set_gather): one task table per gathered buffer
     Task *gtable[2] = {nullptr, nullptr};
     GatherSignal sig{};
     uint32_t epoch = 0;
     bool gather = false;
 };
+
+namespace {
+q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t xb, const uint8_t *yd,
+                             size_t yb);
+q4rdna_status launch_segments(q4rdna_plan *plan, cudaStream_t cs, const uint8_t *xh, uint8_t *xd, const uint8_t *yd,
+                              uint8_t *yh);
+}  // namespace
 
 extern "C" {
 
@@ -925,6 +950,14 @@ q4rdna_status q4rdna_plan_run(q4rdna_plan *plan, q4rdna_stream_t stream) {
     if (plan == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev != plan->device) return Q4RDNA_ERR_DEVICE;
+    if (!plan->gather && plan->run_segments > 1) {
+        const int want = std::min(plan->run_segments, plan->count);
+        if (plan->seg_request != want) {
+            const q4rdna_status st = build_segments(plan, want, nullptr, 0, nullptr, 0);
+            if (st != Q4RDNA_OK) return st;
+        }
+        return launch_segments(plan, (cudaStream_t)stream, nullptr, nullptr, nullptr, nullptr);
+    }
     Launch L{};
     L.table = plan->table;
     L.ntasks = plan->count;
@@ -993,6 +1026,185 @@ q4rdna_status q4rdna_plan_set_gather(q4rdna_plan *plan, int world, int rank, con
     return Q4RDNA_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+// Cuts the plan into `want` runs of consecutive tasks with about equal weight
+// bytes and gives each its own device task table, events and byte ranges.
+q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t xb, const uint8_t *yd,
+                             size_t yb) {
+    for (auto &sg : p->segs) {
+        if (sg.table) cudaFree(sg.table);
+        if (sg.x_ready) cudaEventDestroy(sg.x_ready);
+        if (sg.y_ready) cudaEventDestroy(sg.y_ready);
+    }
+    p->segs.clear();
+    p->seg_request = -1;
+    DeviceInfo d;
+    if (!device_info(d)) return Q4RDNA_ERR_DEVICE;
+    const int n = p->count;
+    want = std::max(1, std::min(want, n));
+    uint64_t total = 0;
+    for (const Task &T : p->host) total += (uint64_t)T.N * T.K * (T.op == Q4RDNA_OP_SWIGLU ? 2 : 1);
+    int first = 0;
+    uint64_t acc = 0;
+    for (int s = 0; s < want && first < n; ++s) {
+        int last = first;  // exclusive end
+        const uint64_t goal = total * (uint64_t)(s + 1) / (uint64_t)want;
+        while (last < n && (last == first || acc < goal || s == want - 1)) {
+            const Task &T = p->host[last];
+            acc += (uint64_t)T.N * T.K * (T.op == Q4RDNA_OP_SWIGLU ? 2 : 1);
+            ++last;
+        }
+        q4rdna_plan::Segment sg;
+        sg.first = first;
+        sg.count = last - first;
+        sg.x_lo = sg.y_lo = SIZE_MAX;
+        std::vector<Task> t(p->host.begin() + first, p->host.begin() + last);
+        const long long base = t.front().item_begin;
+        for (Task &T : t) {
+            T.item_begin -= base;
+            const uint8_t *x = reinterpret_cast<const uint8_t *>(T.x);
+            const uint8_t *y = reinterpret_cast<const uint8_t *>(T.y);
+            const size_t xn = (size_t)p->B * T.K * sizeof(float), yn = (size_t)p->B * T.N * sizeof(float);
+            if (xd == nullptr) continue;  // device-only segments: no copy ranges
+            if (x < xd || x + xn > xd + xb || y < yd || y + yn > yd + yb) return Q4RDNA_ERR_INVALID_ARGUMENT;
+            sg.x_lo = std::min(sg.x_lo, (size_t)(x - xd));
+            sg.x_hi = std::max(sg.x_hi, (size_t)(x - xd) + xn);
+            sg.y_lo = std::min(sg.y_lo, (size_t)(y - yd));
+            sg.y_hi = std::max(sg.y_hi, (size_t)(y - yd) + yn);
+        }
+        const long long end = last < n ? p->host[last].item_begin : p->items;
+        sg.items = end - base;
+        sg.grid = grid_for(sg.items, p->B, p->dual, d);
+        p->segs.push_back(sg);  // owned by the plan from here on (freed on failure paths below)
+        q4rdna_plan::Segment &g = p->segs.back();
+        if (cudaMalloc(&g.table, sizeof(Task) * t.size()) != cudaSuccess ||
+            cudaMemcpy(g.table, t.data(), sizeof(Task) * t.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaEventCreateWithFlags(&g.x_ready, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&g.y_ready, cudaEventDisableTiming) != cudaSuccess)
+            return Q4RDNA_ERR_CUDA;
+        first = last;
+    }
+    // the segments' ranges must be disjoint: a later segment's input copy may
+    // land while an earlier segment still reads, and outputs leave early
+    for (size_t a = 0; xd != nullptr && a < p->segs.size(); ++a)
+        for (size_t b = a + 1; b < p->segs.size(); ++b) {
+            const auto &A = p->segs[a], &Bs = p->segs[b];
+            if (A.x_lo < Bs.x_hi && Bs.x_lo < A.x_hi) return Q4RDNA_ERR_INVALID_ARGUMENT;
+            if (A.y_lo < Bs.y_hi && Bs.y_lo < A.y_hi) return Q4RDNA_ERR_INVALID_ARGUMENT;
+        }
+    if (p->h2d == nullptr &&
+        (cudaStreamCreateWithFlags(&p->h2d, cudaStreamNonBlocking) != cudaSuccess ||
+         cudaStreamCreateWithFlags(&p->d2h, cudaStreamNonBlocking) != cudaSuccess ||
+         cudaStreamCreateWithFlags(&p->comp[0], cudaStreamNonBlocking) != cudaSuccess ||
+         cudaStreamCreateWithFlags(&p->comp[1], cudaStreamNonBlocking) != cudaSuccess ||
+         cudaEventCreateWithFlags(&p->start, cudaEventDisableTiming) != cudaSuccess ||
+         cudaEventCreateWithFlags(&p->done, cudaEventDisableTiming) != cudaSuccess))
+        return Q4RDNA_ERR_CUDA;
+    p->seg_request = want;
+    p->seg_x = xd;
+    p->seg_y = yd;
+    return Q4RDNA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+}  // extern "C"
+
+namespace {
+
+// Runs the plan's segments, alternating between the two library streams, after
+// prior work on cs; cs waits for the end.  With host buffers (xh != null) each
+// segment's input copy precedes it on the copy stream and its output copy
+// follows it on the other copy stream.
+q4rdna_status launch_segments(q4rdna_plan *plan, cudaStream_t cs, const uint8_t *xh, uint8_t *xd, const uint8_t *yd,
+                              uint8_t *yh) {
+    const bool copies = xh != nullptr;
+    if (cudaEventRecord(plan->start, cs) != cudaSuccess ||
+        cudaStreamWaitEvent(plan->comp[0], plan->start, 0) != cudaSuccess ||
+        cudaStreamWaitEvent(plan->comp[1], plan->start, 0) != cudaSuccess)
+        return Q4RDNA_ERR_CUDA;
+    if (copies && (cudaStreamWaitEvent(plan->h2d, plan->start, 0) != cudaSuccess ||
+                   cudaStreamWaitEvent(plan->d2h, plan->start, 0) != cudaSuccess))
+        return Q4RDNA_ERR_CUDA;
+    for (auto &sg : plan->segs) {
+        if (!copies) break;
+        if (cudaMemcpyAsync(xd + sg.x_lo, xh + sg.x_lo, sg.x_hi - sg.x_lo, cudaMemcpyHostToDevice, plan->h2d) !=
+                cudaSuccess ||
+            cudaEventRecord(sg.x_ready, plan->h2d) != cudaSuccess)
+            return Q4RDNA_ERR_CUDA;
+    }
+    for (size_t i = 0; i < plan->segs.size(); ++i) {
+        auto &sg = plan->segs[i];
+        // segments alternate between two streams: segment i + 1 starts on the
+        // SMs that segment i's last items leave idle
+        cudaStream_t c = plan->comp[i & 1];
+        if (copies && cudaStreamWaitEvent(c, sg.x_ready, 0) != cudaSuccess) return Q4RDNA_ERR_CUDA;
+        Launch L{};
+        L.table = sg.table;
+        L.ntasks = sg.count;
+        L.B = plan->B;
+        L.total_items = sg.items;
+        const q4rdna_status st = launch(L, sg.grid, plan->nb, plan->dual, c);
+        if (st != Q4RDNA_OK) return st;
+        if (cudaEventRecord(sg.y_ready, c) != cudaSuccess) return Q4RDNA_ERR_CUDA;
+        if (!copies) continue;
+        if (cudaStreamWaitEvent(plan->d2h, sg.y_ready, 0) != cudaSuccess ||
+            cudaMemcpyAsync(yh + sg.y_lo, yd + sg.y_lo, sg.y_hi - sg.y_lo, cudaMemcpyDeviceToHost, plan->d2h) !=
+                cudaSuccess)
+            return Q4RDNA_ERR_CUDA;
+    }
+    if (copies) {
+        if (cudaEventRecord(plan->done, plan->d2h) != cudaSuccess || cudaStreamWaitEvent(cs, plan->done, 0) != cudaSuccess)
+            return Q4RDNA_ERR_CUDA;
+    } else {
+        // the last segment of each stream ends that stream's work
+        const size_t n = plan->segs.size();
+        for (size_t i = n >= 2 ? n - 2 : 0; i < n; ++i)
+            if (cudaStreamWaitEvent(cs, plan->segs[i].y_ready, 0) != cudaSuccess) return Q4RDNA_ERR_CUDA;
+    }
+    return Q4RDNA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *x_dev, size_t x_bytes,
+                                   const void *y_dev, void *y_host, size_t y_bytes, int segments,
+                                   q4rdna_stream_t stream) {
+    if (plan == nullptr || x_host == nullptr || x_dev == nullptr || y_dev == nullptr || y_host == nullptr ||
+        segments < 0)
+        return Q4RDNA_ERR_INVALID_ARGUMENT;
+    if (plan->gather) return Q4RDNA_ERR_UNSUPPORTED;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != plan->device) return Q4RDNA_ERR_DEVICE;
+    const int want = segments == 0 ? kDefaultSegments : segments;
+    if (plan->seg_request != std::max(1, std::min(want, plan->count)) || plan->seg_x != x_dev ||
+        plan->seg_y != y_dev) {
+        const q4rdna_status st = build_segments(plan, want, static_cast<const uint8_t *>(x_dev), x_bytes,
+                                                static_cast<const uint8_t *>(y_dev), y_bytes);
+        if (st != Q4RDNA_OK) return st;
+    } else {
+        for (const auto &sg : plan->segs)
+            if (sg.x_hi > x_bytes || sg.y_hi > y_bytes) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    }
+    return launch_segments(plan, (cudaStream_t)stream, static_cast<const uint8_t *>(x_host),
+                           static_cast<uint8_t *>(x_dev), static_cast<const uint8_t *>(y_dev),
+                           static_cast<uint8_t *>(y_host));
+}
+
+q4rdna_status q4rdna_plan_set_segments(q4rdna_plan *plan, int segments) {
+    if (plan == nullptr || segments < 0) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    if (plan->gather) return Q4RDNA_ERR_UNSUPPORTED;
+    plan->run_segments = segments == 0 ? kDefaultSegments : segments;
+    return Q4RDNA_OK;
+}
+
 int q4rdna_plan_gather_parity(const q4rdna_plan *plan) {
     if (plan == nullptr || !plan->gather || plan->epoch == 0) return -1;
     return (int)(plan->epoch & 1u);
@@ -1048,6 +1260,17 @@ q4rdna_status q4rdna_plan_get_info(const q4rdna_plan *plan, q4rdna_plan_info *in
 void q4rdna_plan_destroy(q4rdna_plan *plan) {
     if (plan == nullptr) return;
     if (plan->table) cudaFree(plan->table);
+    for (auto &sg : plan->segs) {
+        if (sg.table) cudaFree(sg.table);
+        if (sg.x_ready) cudaEventDestroy(sg.x_ready);
+        if (sg.y_ready) cudaEventDestroy(sg.y_ready);
+    }
+    if (plan->h2d) cudaStreamDestroy(plan->h2d);
+    for (cudaStream_t c : plan->comp)
+        if (c) cudaStreamDestroy(c);
+    if (plan->d2h) cudaStreamDestroy(plan->d2h);
+    if (plan->start) cudaEventDestroy(plan->start);
+    if (plan->done) cudaEventDestroy(plan->done);
     for (Task *t : plan->gtable)
         if (t) cudaFree(t);
     if (plan->workspace) cudaFree(plan->workspace);

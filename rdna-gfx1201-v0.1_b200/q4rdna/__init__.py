@@ -66,6 +66,8 @@ def _bind(lib):
         "q4rdna_plan_run": (c_int, [P, P]),
         "q4rdna_plan_get_info": (c_int, [P, POINTER(PlanInfo)]),
         "q4rdna_plan_destroy": (None, [P]),
+        "q4rdna_plan_run_host": (c_int, [P, P, P, c_size_t, P, P, c_size_t, c_int, P]),
+        "q4rdna_plan_set_segments": (c_int, [P, c_int]),
         "q4rdna_plan_set_gather": (c_int, [P, c_int, c_int, P, c_size_t, POINTER(P), POINTER(P), POINTER(P)]),
         "q4rdna_plan_gather_parity": (c_int, [P]),
         "q4rdna_ipc_alloc": (c_int, [c_size_t, POINTER(P), ctypes.c_char_p]),
@@ -100,7 +102,7 @@ SYMBOLS = [
     "q4rdna_workspace_init", "q4rdna_gemv", "q4rdna_gemv_add", "q4rdna_gemv_swiglu", "q4rdna_dequant_f32",
     "q4rdna_gemv_noalloc",
     "q4rdna_plan_create", "q4rdna_plan_run", "q4rdna_plan_get_info", "q4rdna_plan_destroy",
-    "q4rdna_plan_set_gather", "q4rdna_plan_gather_parity", "q4rdna_ipc_alloc", "q4rdna_ipc_open",
+    "q4rdna_plan_run_host", "q4rdna_plan_set_segments", "q4rdna_plan_set_gather", "q4rdna_plan_gather_parity", "q4rdna_ipc_alloc", "q4rdna_ipc_open",
     "q4rdna_ipc_close", "q4rdna_ipc_free",
     "q4rdna_sidecar_open", "q4rdna_sidecar_close", "q4rdna_sidecar_count", "q4rdna_sidecar_entry",
     "q4rdna_sidecar_find", "q4rdna_mul_mat", "q4rdna_mul_mat_add", "q4rdna_mul_mat_glu",
@@ -251,6 +253,25 @@ class Plan:
 
     def run(self, stream=None):
         check(_lib().q4rdna_plan_run(self._h, _stream_handle(stream)), "plan_run")
+
+    def set_segments(self, segments: int):
+        """run() as `segments` overlapping launches (q4rdna_plan_set_segments;
+        1 = one launch, 0 = the library default of 16)."""
+        check(_lib().q4rdna_plan_set_segments(self._h, segments), "plan_set_segments")
+
+    def run_host(self, x_host, x_dev, y_dev, y_host, segments: int = 0, stream=None):
+        """One run from host memory (q4rdna_plan_run_host): x_host -> x_dev,
+        the GEMVs, y_dev -> y_host, in `segments` overlapped pieces (0: 16).
+        x_dev / y_dev must contain every descriptor's x / y; the host tensors
+        (pinned) mirror them byte for byte."""
+        for t in (x_host, x_dev, y_dev, y_host):
+            if not t.is_contiguous():
+                raise ValueError("run_host needs contiguous buffers")
+        if x_host.nbytes != x_dev.nbytes or y_host.nbytes != y_dev.nbytes:
+            raise ValueError("host and device buffers differ in size")
+        check(_lib().q4rdna_plan_run_host(self._h, x_host.data_ptr(), x_dev.data_ptr(), x_dev.nbytes,
+                                          y_dev.data_ptr(), y_host.data_ptr(), y_dev.nbytes, segments,
+                                          _stream_handle(stream)), "plan_run_host")
 
     def info(self) -> dict:
         i = PlanInfo()
