@@ -242,8 +242,7 @@ def run_ours(args):
     descs, x_all, y_all, wbytes, abytes, ntensors, lay = build_step(args.model, rank, world, dev, args.seed,
                                                                    args.layers, B)
     plan = q4rdna.Plan(descs, B=B)
-    if world == 1:
-        plan.set_segments(args.run_segments)
+    plan.set_segments(args.run_segments)
     info = plan.info()
     stream = torch.cuda.current_stream()
     p2p = world > 1 and args.gather == "p2p"
@@ -399,7 +398,7 @@ def main():
     ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
                     help="N > 1: all-gather fused into the plan kernel (p2p) or one NCCL all-gather per step")
     ap.add_argument("--run-segments", type=int, default=0,
-                    help="N = 1: device-resident step as this many overlapping launches (0: library default, 1: one launch)")
+                    help="device-resident step as this many overlapping launches (0: library default, 1: one launch)")
     ap.add_argument("--segments", type=int, default=0,
                     help="e2e leg at N = 1: plan segments whose host copies overlap the GEMVs (0: library default)")
     ap.add_argument("--batch", type=int, default=1,

@@ -755,7 +755,16 @@ __global__ void q4_gather_signal_kernel(const __grid_constant__ GatherSignal a) 
     if (i == kGatherTries) atomicOr(&g_fault, kFaultGatherTimeout);
 }
 
-constexpr int kDefaultSegments = 16;  // plan runs (measured on the Qwen3-8B step: 8..16 best)
+// Default segment count of a plan run: one segment per kSegmentBytes of
+// weights, at most kMaxSegments.  Measured: the Qwen3-8B step (3.69 GB) is
+// fastest as 16 segments (230 MB each); an eighth of it per GPU (461 MB) is
+// 2x slower as 16 segments than as one launch, because every launch has a
+// fixed cost of ~10-15 us that the overlap does not hide.
+constexpr uint64_t kSegmentBytes = 192ull << 20;
+constexpr int kMaxSegments = 16;
+int default_segments(uint64_t weight_bytes) {
+    return (int)std::max<uint64_t>(1, std::min<uint64_t>(kMaxSegments, weight_bytes / kSegmentBytes));
+}
 
 struct q4rdna_plan {
     int device = -1;
@@ -773,18 +782,20 @@ struct q4rdna_plan {
         long long items = 0;
         int grid = 1;
         Task *table = nullptr;  // item_begin rebased to the segment
+        Task *gtable[2] = {nullptr, nullptr};  // the same with the gather's mirrors, per gathered buffer
         size_t x_lo = 0, x_hi = 0, y_lo = 0, y_hi = 0;  // byte ranges from x_dev / y_dev
         cudaEvent_t x_ready = nullptr, y_ready = nullptr;
     };
     std::vector<Segment> segs;
     int seg_request = -1;
-    int run_segments = kDefaultSegments;  // q4rdna_plan_run: 1 = one launch
+    int run_segments = 0;  // q4rdna_plan_run: 0 = default_segments(weight_bytes), 1 = one launch
     const void *seg_x = nullptr, *seg_y = nullptr;
     cudaStream_t h2d = nullptr, d2h = nullptr;
     cudaStream_t comp[2] = {nullptr, nullptr};  // segments alternate, so one's tail overlaps the next
     cudaEvent_t start = nullptr, done = nullptr;
     // fused gather (q4rdna_plan_set_gather): one task table per gathered buffer
     Task *gtable[2] = {nullptr, nullptr};
+    std::vector<Task> ghost[2];
     GatherSignal sig{};
     uint32_t epoch = 0;
     bool gather = false;
@@ -794,7 +805,7 @@ namespace {
 q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t xb, const uint8_t *yd,
                              size_t yb);
 q4rdna_status launch_segments(q4rdna_plan *plan, cudaStream_t cs, const uint8_t *xh, uint8_t *xd, const uint8_t *yd,
-                              uint8_t *yh);
+                              uint8_t *yh, int par = -1);
 }  // namespace
 
 extern "C" {
@@ -950,23 +961,36 @@ q4rdna_status q4rdna_plan_run(q4rdna_plan *plan, q4rdna_stream_t stream) {
     if (plan == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev != plan->device) return Q4RDNA_ERR_DEVICE;
-    if (!plan->gather && plan->run_segments > 1) {
-        const int want = std::min(plan->run_segments, plan->count);
+    const int nseg = plan->run_segments > 0 ? plan->run_segments : default_segments(plan->weight_bytes);
+    const bool segmented = nseg > 1 && plan->count > 1;
+    if (segmented) {
+        const int want = std::min(nseg, plan->count);
         if (plan->seg_request != want) {
             const q4rdna_status st = build_segments(plan, want, nullptr, 0, nullptr, 0);
             if (st != Q4RDNA_OK) return st;
         }
-        return launch_segments(plan, (cudaStream_t)stream, nullptr, nullptr, nullptr, nullptr);
     }
-    Launch L{};
-    L.table = plan->table;
-    L.ntasks = plan->count;
-    L.B = plan->B;
-    L.total_items = plan->items;
-    if (!plan->gather) return launch(L, plan->grid, plan->nb, plan->dual, (cudaStream_t)stream);
+    if (!plan->gather) {
+        if (segmented) return launch_segments(plan, (cudaStream_t)stream, nullptr, nullptr, nullptr, nullptr);
+        Launch L{};
+        L.table = plan->table;
+        L.ntasks = plan->count;
+        L.B = plan->B;
+        L.total_items = plan->items;
+        return launch(L, plan->grid, plan->nb, plan->dual, (cudaStream_t)stream);
+    }
     const uint32_t epoch = plan->epoch + 1;
-    L.table = plan->gtable[epoch & 1];
-    q4rdna_status st = launch(L, plan->grid, plan->nb, plan->dual, (cudaStream_t)stream);
+    q4rdna_status st;
+    if (segmented) {
+        st = launch_segments(plan, (cudaStream_t)stream, nullptr, nullptr, nullptr, nullptr, (int)(epoch & 1));
+    } else {
+        Launch L{};
+        L.table = plan->gtable[epoch & 1];
+        L.ntasks = plan->count;
+        L.B = plan->B;
+        L.total_items = plan->items;
+        st = launch(L, plan->grid, plan->nb, plan->dual, (cudaStream_t)stream);
+    }
     if (st != Q4RDNA_OK) return st;
     GatherSignal sg = plan->sig;
     sg.epoch = epoch;
@@ -1007,6 +1031,7 @@ q4rdna_status q4rdna_plan_set_gather(q4rdna_plan *plan, int world, int rank, con
             T.nmirror = world;
             for (int p = 0; p < world; ++p) T.mirror[p] = g[p] + (size_t)rank * rank_floats + off;
         }
+        plan->ghost[par] = t;
         if (cudaMalloc(&plan->gtable[par], sizeof(Task) * t.size()) != cudaSuccess ||
             cudaMemcpy(plan->gtable[par], t.data(), sizeof(Task) * t.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
             for (Task *&gt : plan->gtable) {
@@ -1023,6 +1048,7 @@ q4rdna_status q4rdna_plan_set_gather(q4rdna_plan *plan, int world, int rank, con
     sg.rank = rank;
     plan->epoch = 0;
     plan->gather = true;
+    plan->seg_request = -1;  // segments are rebuilt with the gather's tables
     return Q4RDNA_OK;
 }
 
@@ -1036,6 +1062,8 @@ q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t
                              size_t yb) {
     for (auto &sg : p->segs) {
         if (sg.table) cudaFree(sg.table);
+        for (Task *t : sg.gtable)
+            if (t) cudaFree(t);
         if (sg.x_ready) cudaEventDestroy(sg.x_ready);
         if (sg.y_ready) cudaEventDestroy(sg.y_ready);
     }
@@ -1085,6 +1113,13 @@ q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t
             cudaEventCreateWithFlags(&g.x_ready, cudaEventDisableTiming) != cudaSuccess ||
             cudaEventCreateWithFlags(&g.y_ready, cudaEventDisableTiming) != cudaSuccess)
             return Q4RDNA_ERR_CUDA;
+        for (int par = 0; p->gather && par < 2; ++par) {
+            std::vector<Task> gt(p->ghost[par].begin() + first, p->ghost[par].begin() + last);
+            for (Task &T : gt) T.item_begin -= base;
+            if (cudaMalloc(&g.gtable[par], sizeof(Task) * gt.size()) != cudaSuccess ||
+                cudaMemcpy(g.gtable[par], gt.data(), sizeof(Task) * gt.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+                return Q4RDNA_ERR_CUDA;
+        }
         first = last;
     }
     // the segments' ranges must be disjoint: a later segment's input copy may
@@ -1122,7 +1157,7 @@ namespace {
 // segment's input copy precedes it on the copy stream and its output copy
 // follows it on the other copy stream.
 q4rdna_status launch_segments(q4rdna_plan *plan, cudaStream_t cs, const uint8_t *xh, uint8_t *xd, const uint8_t *yd,
-                              uint8_t *yh) {
+                              uint8_t *yh, int par) {
     const bool copies = xh != nullptr;
     if (cudaEventRecord(plan->start, cs) != cudaSuccess ||
         cudaStreamWaitEvent(plan->comp[0], plan->start, 0) != cudaSuccess ||
@@ -1145,7 +1180,7 @@ q4rdna_status launch_segments(q4rdna_plan *plan, cudaStream_t cs, const uint8_t 
         cudaStream_t c = plan->comp[i & 1];
         if (copies && cudaStreamWaitEvent(c, sg.x_ready, 0) != cudaSuccess) return Q4RDNA_ERR_CUDA;
         Launch L{};
-        L.table = sg.table;
+        L.table = par >= 0 ? sg.gtable[par] : sg.table;  // par: gathered buffer of a gather run
         L.ntasks = sg.count;
         L.B = plan->B;
         L.total_items = sg.items;
@@ -1183,7 +1218,7 @@ q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *
     if (plan->gather) return Q4RDNA_ERR_UNSUPPORTED;
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev != plan->device) return Q4RDNA_ERR_DEVICE;
-    const int want = segments == 0 ? kDefaultSegments : segments;
+    const int want = segments == 0 ? default_segments(plan->weight_bytes) : segments;
     if (plan->seg_request != std::max(1, std::min(want, plan->count)) || plan->seg_x != x_dev ||
         plan->seg_y != y_dev) {
         const q4rdna_status st = build_segments(plan, want, static_cast<const uint8_t *>(x_dev), x_bytes,
@@ -1200,8 +1235,7 @@ q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *
 
 q4rdna_status q4rdna_plan_set_segments(q4rdna_plan *plan, int segments) {
     if (plan == nullptr || segments < 0) return Q4RDNA_ERR_INVALID_ARGUMENT;
-    if (plan->gather) return Q4RDNA_ERR_UNSUPPORTED;
-    plan->run_segments = segments == 0 ? kDefaultSegments : segments;
+    plan->run_segments = segments;
     return Q4RDNA_OK;
 }
 
@@ -1262,6 +1296,8 @@ void q4rdna_plan_destroy(q4rdna_plan *plan) {
     if (plan->table) cudaFree(plan->table);
     for (auto &sg : plan->segs) {
         if (sg.table) cudaFree(sg.table);
+        for (Task *t : sg.gtable)
+            if (t) cudaFree(t);
         if (sg.x_ready) cudaEventDestroy(sg.x_ready);
         if (sg.y_ready) cudaEventDestroy(sg.y_ready);
     }

@@ -256,12 +256,12 @@ class Plan:
 
     def set_segments(self, segments: int):
         """run() as `segments` overlapping launches (q4rdna_plan_set_segments;
-        1 = one launch, 0 = the library default of 16)."""
+        1 = one launch, 0 = the library default: one per 192 MiB of weights, at most 16)."""
         check(_lib().q4rdna_plan_set_segments(self._h, segments), "plan_set_segments")
 
     def run_host(self, x_host, x_dev, y_dev, y_host, segments: int = 0, stream=None):
         """One run from host memory (q4rdna_plan_run_host): x_host -> x_dev,
-        the GEMVs, y_dev -> y_host, in `segments` overlapped pieces (0: 16).
+        the GEMVs, y_dev -> y_host, in `segments` overlapped pieces (0: the library default).
         x_dev / y_dev must contain every descriptor's x / y; the host tensors
         (pinned) mirror them byte for byte."""
         for t in (x_host, x_dev, y_dev, y_host):
