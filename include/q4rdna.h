@@ -217,6 +217,15 @@ q4rdna_status q4rdna_ipc_close(void *dev_ptr);
 /* Frees a q4rdna_ipc_alloc allocation (after every peer closed its mapping). */
 q4rdna_status q4rdna_ipc_free(void *dev_ptr);
 
+/* Packs a row-major bf16 matrix [N][K] (device memory, 16-byte aligned) into
+ * Q4_RDNA tiles (N*K*34/64 bytes, 2-byte aligned) on the GPU, byte for byte what
+ * the reference packer writes for the tensor.  Replaces the per-tensor loop of
+ * source/q4rdna_sidecar_pack.cpp:262-279 (scale search :140-179, quantiser
+ * :126-129); source/pack_q4rdna_sidecar.py:44-73 writes the same bytes.  The
+ * container (header, entries, alignment) is written by the host
+ * (q4rdna.format.write_sidecar). */
+q4rdna_status q4rdna_pack_bf16(const uint16_t *bf16, uint8_t *tiles, int N, int K, q4rdna_stream_t stream);
+
 /* ---- sidecar (the reference's .q4rdna container, byte layout unchanged) ----
  * Header 48 B, entries 96 B, data at data_offset (source/q4rdna.cu:26-50).
  * Validation follows source/q4rdna.cu:131-152.  The whole data region is

@@ -61,6 +61,7 @@ def _bind(lib):
         "q4rdna_gemv_add": (c_int, [P, P, P, P, c_int, c_int, c_int, POINTER(Cfg), P, c_size_t, P]),
         "q4rdna_gemv_swiglu": (c_int, [P, P, P, P, c_int, c_int, c_int, POINTER(Cfg), P, c_size_t, P]),
         "q4rdna_dequant_f32": (c_int, [P, P, c_int, c_int, P]),
+        "q4rdna_pack_bf16": (c_int, [P, P, c_int, c_int, P]),
         "q4rdna_gemv_noalloc": (c_int, [P, P, P, c_int, c_int, c_int, POINTER(Cfg), P]),
         "q4rdna_plan_create": (c_int, [POINTER(GemvDesc), c_int, c_int, POINTER(P)]),
         "q4rdna_plan_run": (c_int, [P, P]),
@@ -99,7 +100,7 @@ def _bind(lib):
 lib = _bind(ctypes.CDLL(LIB_PATH)) if os.path.exists(LIB_PATH) else None
 SYMBOLS = [
     "q4rdna_status_string", "q4rdna_version", "q4rdna_select_split", "q4rdna_workspace_bytes",
-    "q4rdna_workspace_init", "q4rdna_gemv", "q4rdna_gemv_add", "q4rdna_gemv_swiglu", "q4rdna_dequant_f32",
+    "q4rdna_workspace_init", "q4rdna_gemv", "q4rdna_gemv_add", "q4rdna_gemv_swiglu", "q4rdna_dequant_f32", "q4rdna_pack_bf16",
     "q4rdna_gemv_noalloc",
     "q4rdna_plan_create", "q4rdna_plan_run", "q4rdna_plan_get_info", "q4rdna_plan_destroy",
     "q4rdna_plan_run_host", "q4rdna_plan_set_segments", "q4rdna_plan_set_gather", "q4rdna_plan_gather_parity", "q4rdna_ipc_alloc", "q4rdna_ipc_open",
@@ -223,6 +224,37 @@ def dequant(tiles, N: int, K: int, stream=None):
     W = torch.empty((N, K), dtype=torch.float32, device=tiles.device)
     check(_lib().q4rdna_dequant_f32(tiles.data_ptr(), W.data_ptr(), N, K, _stream_handle(stream)), "dequant")
     return W
+
+
+def pack_bf16(w, stream=None):
+    """Q4_RDNA tiles (uint8 CUDA tensor, N*K*34/64 bytes) of a bf16 matrix
+    [N, K] (torch.bfloat16, or its raw bits as int16/uint16, on the GPU), byte
+    for byte what the reference packer writes (q4rdna_pack_bf16)."""
+    import torch
+
+    if w.dim() != 2 or not w.is_cuda:
+        raise ValueError("pack_bf16 takes a 2-D CUDA tensor")
+    if w.dtype not in (torch.bfloat16, torch.int16, torch.uint16):
+        raise ValueError("pack_bf16 takes bfloat16 weights (or their 16-bit patterns)")
+    w = w.contiguous()
+    N, K = w.shape
+    out = torch.empty(N * K * 34 // 64, dtype=torch.uint8, device=w.device)
+    check(_lib().q4rdna_pack_bf16(w.data_ptr(), out.data_ptr(), N, K, _stream_handle(stream)), "pack_bf16")
+    return out
+
+
+def pack_sidecar(path: str, tensors, stream=None):
+    """Writes a .q4rdna sidecar: tensors is a list of (ggml name, bf16 CUDA
+    tensor [N, K]); every tensor is packed on the GPU and the container is laid
+    out exactly as the reference packer lays it out (q4rdna.format)."""
+    import torch
+
+    packed = []
+    for name, w in tensors:
+        t = pack_bf16(w, stream)
+        packed.append((name, t, w.shape[0], w.shape[1]))
+    torch.cuda.synchronize()
+    return format.write_sidecar(path, [(n, t.cpu().numpy(), r, c) for n, t, r, c in packed])
 
 
 class Plan:
