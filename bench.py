@@ -182,6 +182,78 @@ def reference_cpu_rate(budget_s: float, threads: int):
     return calls * nbytes / el / 1e9, kind, threads, sample
 
 
+def reference_pack_rate(threads: int):
+    """The reference packer binary (q4rdna_sidecar_pack, compiled unmodified
+    from the reference source into oracle/_ref, OpenMP over groups) packing one
+    4096 x 4096 bf16 N(0, 0.02) tensor on `threads` host threads, wall clock.
+    Returns (Gweights/s, sample) or (None, why)."""
+    import numpy as np
+
+    import oracle
+
+    if not os.path.exists(oracle.REF_PACK_BIN):
+        return None, "oracle/_ref/q4rdna_sidecar_pack not built"
+    N, K = 4096, 4096
+    rng = np.random.default_rng(5)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    bits = ((w.view(np.uint32).astype(np.uint64) + 0x7FFF + ((w.view(np.uint32) >> 16) & 1)) >> 16).astype("<u2")
+    with tempfile.TemporaryDirectory() as td:
+        raw = os.path.join(td, "w.bin")
+        bits.tofile(raw)
+        man = os.path.join(td, "m.tsv")
+        with open(man, "w") as f:
+            f.write(f"{raw}\t0\t{N}\t{K}\tblk.0.attn_q.weight\n")
+        env = dict(os.environ, OMP_NUM_THREADS=str(threads))
+        t0 = time.perf_counter()
+        subprocess.run([oracle.REF_PACK_BIN, man, os.path.join(td, "o.q4rdna")], check=True, env=env,
+                       capture_output=True)
+        el = time.perf_counter() - t0
+    return N * K / el / 1e9, f"q4rdna_sidecar_pack, one 4096x4096 bf16 tensor, OpenMP on {threads} threads, {el:.2f} s"
+
+
+def run_pack(args):
+    """GPU packer throughput on the Qwen3-8B weight set: the 7 tensor shapes of
+    a layer, bf16 N(0, 0.02) on the device, each packed once per layer (36 x 7 =
+    252 tensors, 6.95 G weights), timed with CUDA events."""
+    import torch
+
+    import q4rdna
+    from q4rdna import synth
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed)
+    layer = [(N, K) for (_, N, K) in synth.model_tensors(args.model) if _.startswith("blk.0.")]
+    nlayers = len(synth.model_tensors(args.model)) // len(layer)
+    ws = [(torch.randn((N, K), generator=g, device=dev) * 0.02).to(torch.bfloat16) for N, K in layer]
+    for w in ws:  # warm-up
+        q4rdna.pack_bf16(w)
+    torch.cuda.synchronize()
+    l0 = q4rdna.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        e0.record()
+        for _ in range(nlayers):
+            for w in ws:
+                q4rdna.pack_bf16(w)
+        e1.record()
+        torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3
+    weights = nlayers * sum(N * K for N, K in layer)
+    cpu = None
+    if not args.no_cpu_baseline:
+        v, sample = reference_pack_rate(cpu_count())
+        if v is not None:
+            cpu = {"value": round(v, 4), "unit": "Gweights/s", "cores": cpu_count(), "kind": "reference",
+                   "sample": sample, "model_seconds": round(weights / (v * 1e9), 1)}
+    return {"metric": f"Q4_RDNA sidecar packing of {args.model} (bf16 -> tiles), Gweights/s",
+            "value": round(weights / sec / 1e9, 3), "unit": "Gweights/s", "model_seconds": round(sec, 3),
+            "n_gpus": 1, "higher_is_better": True, "dtype": "bf16 in, int4 + fp16 scales out",
+            "data": "synthetic: bf16 N(0, 0.02) weights of the model's shapes (no Qwen3 weights offline)",
+            "config": {"workload": f"{nlayers} layers x {len(layer)} tensors, {weights} weights"},
+            "cpu_baseline": cpu, "gpu_launches": q4rdna.launch_count() - l0, "clocks": clk.summary()}
+
+
 def build_step(model: str, rank: int, world: int, device, seed: int, layers: int = 0, B: int = 1):
     """Weights (this rank's row shard of every tensor), activations and outputs
     of one decode step, laid out by q4rdna.tp.Layout so that a step's inputs and
@@ -397,6 +469,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
                     help="N > 1: all-gather fused into the plan kernel (p2p) or one NCCL all-gather per step")
+    ap.add_argument("--pack", action="store_true",
+                    help="time the GPU sidecar packer on the model's weights instead of the GEMV step")
     ap.add_argument("--run-segments", type=int, default=0,
                     help="device-resident step as this many overlapping launches (0: library default, 1: one launch)")
     ap.add_argument("--segments", type=int, default=0,
@@ -413,7 +487,10 @@ def main():
     sys.stdout.flush()
     result = os.fdopen(os.dup(1), "w")
     os.dup2(2, 1)
-    out = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if args.pack:
+        out = run_pack(args)
+    else:
+        out = run_reference(args) if args.impl == "reference" else run_ours(args)
     if out is not None:
         print(json.dumps(out), file=result, flush=True)
 

@@ -30,11 +30,16 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <climits>
 #include <cstdint>
 
 #include "q4rdna.h"
 #include "q4rdna_tile.h"
+
+namespace q4 {
+extern std::atomic<uint64_t> g_launches;  // q4rdna_gemv.cu: kernels launched by the library
+}
 
 namespace q4pack {
 
@@ -220,5 +225,7 @@ extern "C" q4rdna_status q4rdna_pack_bf16(const uint16_t *bf16, uint8_t *tiles, 
     const long long blocks = (ntiles + 3) / 4;
     if (blocks > INT_MAX) return Q4RDNA_ERR_TOO_LARGE;
     q4pack::q4_pack_bf16_kernel<<<(unsigned)blocks, 128, 0, (cudaStream_t)stream>>>(bf16, tiles, N, K);
-    return cudaGetLastError() == cudaSuccess ? Q4RDNA_OK : Q4RDNA_ERR_CUDA;
+    if (cudaGetLastError() != cudaSuccess) return Q4RDNA_ERR_CUDA;
+    q4::g_launches.fetch_add(1, std::memory_order_relaxed);
+    return Q4RDNA_OK;
 }
