@@ -96,6 +96,23 @@ q4rdna_status q4rdna_gemv_swiglu(const uint8_t *up_tiles, const uint8_t *gate_ti
                                  float *y, int N, int K, int B, const q4rdna_cfg *cfg,
                                  void *workspace, size_t workspace_bytes, q4rdna_stream_t stream);
 
+/* The GEMV with its input produced by RMSNorm in the same kernel:
+ *   y = W (h * g) / sqrt(mean(h^2) + eps) [+ add | * silu(...) for SwiGLU]
+ * per batch column, h f32 [B][K] the raw hidden state, g = norm_weight f32 [K]
+ * (8-byte aligned).  This is the ggml rms_norm + mul pair that feeds the
+ * reference's mul_mat nodes (the llama.cpp graph before
+ * llama-cpp-q4rdna-integration.patch:17-19), fused into the weight stream: the
+ * sum of h^2 is taken while the activation groups are prepared, and the scale
+ * is applied once per output (after the split-K reduction when S > 1, splits
+ * in ascending order).  op, gate_tiles and add as in q4rdna_gemv_swiglu /
+ * q4rdna_gemv_add; the workspace is sized by q4rdna_workspace_bytes.  Runs on
+ * the default kernels only (Q4RDNA_ERR_UNSUPPORTED under Q4RDNA_KERNEL=ldg or
+ * i8tma at B <= 2). */
+q4rdna_status q4rdna_gemv_rmsnorm(const uint8_t *tiles, const uint8_t *gate_tiles, const float *h,
+                                  const float *norm_weight, float eps, const float *add, float *y, int N, int K,
+                                  int B, int op, const q4rdna_cfg *cfg, void *workspace, size_t workspace_bytes,
+                                  q4rdna_stream_t stream);
+
 /* y = W x without any allocation and without a workspace argument.  No
  * counterpart in the reference.  For callers that cannot call cudaMalloc: an
  * operator hook inside a host framework (like the llama.cpp mul_mat hook) gets
@@ -136,6 +153,9 @@ typedef struct q4rdna_gemv_desc {
     int K;
     int op;
     int split; /* 0 = selector */
+    /* fused RMSNorm (q4rdna_gemv_rmsnorm): norm weight [K] or NULL; x is then the raw input h */
+    const float *norm_weight;
+    float norm_eps;
 } q4rdna_gemv_desc;
 
 typedef struct q4rdna_plan q4rdna_plan;

@@ -68,6 +68,10 @@ struct Task {
     int N, K, G, RB, S, Gs, op;
     int nmirror;        // tensor-parallel gather: copies of y in every rank's gathered buffer
     long long item_begin;
+    const float *gn;    // fused RMSNorm: the norm weight [K] (x is then the raw input h), else null
+    float eps;          // fused RMSNorm: y = W (h * g) / sqrt(mean(h^2) + eps)
+    int pad2;
+    float *nss;         // fused RMSNorm with S > 1: sums of h^2 per [RB][S][B]
     float *mirror[kMaxMirrors];  // [B][N] each, on this GPU or a peer (plain P2P stores)
 };
 
@@ -265,9 +269,23 @@ __device__ __forceinline__ float finish(float v, float gate, int op, const float
     return v;
 }
 
+// Fused RMSNorm: the output scale 1 / sqrt(mean(h^2) + eps) from the sum of h^2
+// over all K columns (ggml_rms_norm's definition).
+__device__ __forceinline__ float norm_scale(const Task &T, float sumsq) {
+    return 1.0f / sqrtf(sumsq / (float)T.K + T.eps);
+}
+
+// Fused RMSNorm, S > 1: the sum of h^2 of batch column b over the row block's
+// splits, in ascending split order.
+__device__ __forceinline__ float split_sumsq(const Task &T, int rb, int b, int B) {
+    float s = 0.0f;
+    for (int sp = 0; sp < T.S; ++sp) s += __ldcg(&T.nss[((size_t)rb * T.S + sp) * B + b]);
+    return s;
+}
+
 // Last warp to arrive at row block rb: add the split partials in ascending
 // split order, apply the epilogue, store y, and leave the ticket at zero.
-template <bool DUAL>
+template <bool DUAL, bool NORM = false>
 __device__ __forceinline__ void reduce_splits(const Task &T, int rb, int B, int lane) {
     constexpr int planes = DUAL ? 2 : 1;
     __threadfence();
@@ -282,6 +300,11 @@ __device__ __forceinline__ void reduce_splits(const Task &T, int rb, int B, int 
             for (int sp = 0; sp < T.S; ++sp) {
                 s0 += __ldcg(p0 + sp * split_stride);
                 if (DUAL) s1 += __ldcg(p0 + sp * split_stride + (size_t)B * T.N);
+            }
+            if (NORM && T.gn != nullptr) {
+                const float r = norm_scale(T, split_sumsq(T, rb, b, B));
+                s0 *= r;
+                s1 *= r;
             }
             const size_t idx = (size_t)b * T.N + row;
             put_y(T, idx, finish(s0, s1, T.op, T.add, idx));
@@ -499,19 +522,26 @@ int batch_class(int pb) { return pb <= 1 ? 0 : pb == 2 ? 1 : pb <= 4 ? 2 : pb <=
 int class_batch(int bc) { return bc == 0 ? 1 : bc == 1 ? 2 : bc == 2 ? 4 : bc == 3 ? 8 : 16; }
 
 // Tile path for B = 5..16 (q4rdna_gemv_mb.cuh): one work item per CTA.
-KernelCfg mb_cfg(int pb, bool dual) {
+template <bool NORM>
+KernelCfg mb_cfg_n(int pb, bool dual) {
     if (pb <= 8)
-        return dual ? KernelCfg{(const void *)q4_gemv_mb_kernel<8, true>, kMbThreads, 0, 1}
-                    : KernelCfg{(const void *)q4_gemv_mb_kernel<8, false>, kMbThreads, 0, 1};
-    return dual ? KernelCfg{(const void *)q4_gemv_mb_kernel<16, true>, kMbThreads, 0, 1}
-                : KernelCfg{(const void *)q4_gemv_mb_kernel<16, false>, kMbThreads, 0, 1};
+        return dual ? KernelCfg{(const void *)q4_gemv_mb_kernel<8, true, NORM>, kMbThreads, 0, 1}
+                    : KernelCfg{(const void *)q4_gemv_mb_kernel<8, false, NORM>, kMbThreads, 0, 1};
+    return dual ? KernelCfg{(const void *)q4_gemv_mb_kernel<16, true, NORM>, kMbThreads, 0, 1}
+                : KernelCfg{(const void *)q4_gemv_mb_kernel<16, false, NORM>, kMbThreads, 0, 1};
 }
+KernelCfg mb_cfg(int pb, bool dual, bool norm) { return norm ? mb_cfg_n<true>(pb, dual) : mb_cfg_n<false>(pb, dual); }
 
 template <bool DUAL>
-KernelCfg i8_cfg(int pb) {
-    if (pb <= 1) return KernelCfg{(const void *)q4_gemv_i8_kernel<1, DUAL>, kThreads, 0, kWarps};
-    if (pb == 2) return KernelCfg{(const void *)q4_gemv_i8_kernel<2, DUAL>, kThreads, 0, kWarps};
-    return KernelCfg{(const void *)q4_gemv_i8_kernel<4, DUAL>, kThreads, 0, kWarps};
+KernelCfg i8_cfg(int pb, bool norm) {
+    if (norm) {
+        if (pb <= 1) return KernelCfg{(const void *)q4_gemv_i8_kernel<1, DUAL, true>, kThreads, 0, kWarps};
+        if (pb == 2) return KernelCfg{(const void *)q4_gemv_i8_kernel<2, DUAL, true>, kThreads, 0, kWarps};
+        return KernelCfg{(const void *)q4_gemv_i8_kernel<4, DUAL, true>, kThreads, 0, kWarps};
+    }
+    if (pb <= 1) return KernelCfg{(const void *)q4_gemv_i8_kernel<1, DUAL, false>, kThreads, 0, kWarps};
+    if (pb == 2) return KernelCfg{(const void *)q4_gemv_i8_kernel<2, DUAL, false>, kThreads, 0, kWarps};
+    return KernelCfg{(const void *)q4_gemv_i8_kernel<4, DUAL, false>, kThreads, 0, kWarps};
 }
 
 KernelCfg i8tma_cfg(int pb) {
@@ -535,14 +565,16 @@ int tile_min_batch() {
     return v;
 }
 
-KernelCfg kernel_cfg(int v, int pb, bool dual = true) {
-    if (pb >= tile_min_batch()) return mb_cfg(pb, dual);
+// norm: the launch holds a fused-RMSNorm task (occupancy and grids are taken
+// from the kernels without it; the norm kernels use the same registers +- 5).
+KernelCfg kernel_cfg(int v, int pb, bool dual = true, bool norm = false) {
+    if (pb >= tile_min_batch()) return mb_cfg(pb, dual, norm);
     switch (v) {
         case kI8Tma: return i8tma_cfg(pb);
         case kLdg:
             return pb <= 2 ? KernelCfg{(const void *)q4_gemv_kernel<1>, kThreads, 0, kWarps}
                            : KernelCfg{(const void *)q4_gemv_kernel<2>, kThreads, 0, kWarps};
-        default: return dual ? i8_cfg<true>(pb) : i8_cfg<false>(pb);
+        default: return dual ? i8_cfg<true>(pb, norm) : i8_cfg<false>(pb, norm);
     }
 }
 
@@ -635,17 +667,30 @@ size_t partial_bytes(int N, int B, int S, int op) {
     return (size_t)S * planes * B * N * sizeof(float);
 }
 
-// Workspace of one q4rdna_gemv* call: ticket area + partials (0 when S == 1).
-size_t ws_bytes_for(int N, int B, int S, int op) {
-    return S <= 1 ? 0 : kTicketArea + partial_bytes(N, B, S, op);
+// Fused RMSNorm with S > 1: one sum of h^2 per (row block, split, batch column).
+size_t sumsq_bytes(int N, int B, int S) {
+    const int RB = (N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
+    return (size_t)RB * S * B * sizeof(float);
 }
 
-// Workspace of one plan task: its own tickets + partials (fixed for the plan's life).
-size_t plan_ws_bytes_for(int N, int B, int S, int op) {
+// Workspace of one q4rdna_gemv* call: ticket area + partials + the RMSNorm sums
+// (reserved for every call, so one size query serves both; 0 when S == 1).
+size_t ws_bytes_for(int N, int B, int S, int op) {
+    return S <= 1 ? 0 : kTicketArea + partial_bytes(N, B, S, op) + sumsq_bytes(N, B, S);
+}
+
+// Workspace of one plan task: its own tickets + partials (+ RMSNorm sums), fixed
+// for the plan's life.
+size_t plan_ws_bytes_for(int N, int B, int S, int op, bool norm) {
     if (S <= 1) return 0;
     const int RB = (N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
-    return align256((size_t)RB * sizeof(unsigned)) + align256(partial_bytes(N, B, S, op));
+    return align256((size_t)RB * sizeof(unsigned)) + align256(partial_bytes(N, B, S, op)) +
+           (norm ? align256(sumsq_bytes(N, B, S)) : 0);
 }
+
+// The fused RMSNorm runs in the int8 batch-1 kernel and the tile path, not in
+// the A/B variants (Q4RDNA_KERNEL=ldg|i8tma).
+bool norm_supported(int B) { return B >= tile_min_batch() || variant() == kI8; }
 
 bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
@@ -664,8 +709,8 @@ int grid_for(long long items, int pb, bool dual, const DeviceInfo &d) {
 }
 
 // pb: batch columns of the launch (1..16).
-q4rdna_status launch(const Launch &L, int grid, int pb, bool dual, cudaStream_t stream) {
-    const KernelCfg k = kernel_cfg(variant(), pb, dual);
+q4rdna_status launch(const Launch &L, int grid, int pb, bool dual, cudaStream_t stream, bool norm = false) {
+    const KernelCfg k = kernel_cfg(variant(), pb, dual, norm);
     Launch arg = L;
     void *args[] = {&arg};
     if (cudaLaunchKernel(k.fn, dim3(grid), dim3(k.threads), args, (size_t)k.smem, stream) != cudaSuccess)
@@ -677,14 +722,16 @@ q4rdna_status launch(const Launch &L, int grid, int pb, bool dual, cudaStream_t 
 
 q4rdna_status gemv_common(int op, const uint8_t *w, const uint8_t *w2, const float *x, const float *add, float *y,
                           int N, int K, int B, const q4rdna_cfg *cfg, void *ws, size_t ws_bytes,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, const float *gn = nullptr, float eps = 0.0f) {
     q4rdna_status st = check_shape(N, K, B);
     if (st != Q4RDNA_OK) return st;
     if (w == nullptr || x == nullptr || y == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
     if (op == Q4RDNA_OP_ADD && add == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
     if (op == Q4RDNA_OP_SWIGLU && w2 == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
-    if (!aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(x, 8) || !aligned(y, 4) || (add && !aligned(add, 4)))
+    if (!aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(x, 8) || !aligned(y, 4) || (add && !aligned(add, 4)) ||
+        (gn && !aligned(gn, 8)))
         return Q4RDNA_ERR_ALIGNMENT;
+    if (gn != nullptr && !norm_supported(B)) return Q4RDNA_ERR_UNSUPPORTED;
     DeviceInfo d;
     if (!device_info(d)) return Q4RDNA_ERR_DEVICE;
     const int G = K / Q4_GROUP;
@@ -715,11 +762,12 @@ q4rdna_status gemv_common(int op, const uint8_t *w, const uint8_t *w2, const flo
     T.ticket = ticket;
     T.N = N; T.K = K; T.G = G; T.RB = RB; T.S = sp.S; T.Gs = sp.Gs; T.op = op; T.nmirror = 0;
     T.item_begin = 0;
+    T.gn = gn;
+    T.eps = eps;
+    T.nss = (gn != nullptr && sp.S > 1) ? part + partial_bytes(N, B, sp.S, op) / sizeof(float) : nullptr;
     L.total_items = (long long)RB * sp.S;
     const bool dual = op == Q4RDNA_OP_SWIGLU;
-    st = launch(L, grid_for(L.total_items, B, dual, d), B, dual, stream);
-    if (st != Q4RDNA_OK) return st;
-    return Q4RDNA_OK;
+    return launch(L, grid_for(L.total_items, B, dual, d), B, dual, stream, gn != nullptr);
 }
 
 }  // namespace q4
@@ -770,6 +818,7 @@ struct q4rdna_plan {
     int device = -1;
     int count = 0, B = 1, nb = 1, grid = 1;
     bool dual = false;  // the plan holds a SwiGLU task
+    bool norm = false;  // the plan holds a fused-RMSNorm task
     long long items = 0;
     Task *table = nullptr;     // device
     void *workspace = nullptr; // device
@@ -870,6 +919,16 @@ q4rdna_status q4rdna_gemv_swiglu(const uint8_t *up_tiles, const uint8_t *gate_ti
                        workspace_bytes, (cudaStream_t)stream);
 }
 
+q4rdna_status q4rdna_gemv_rmsnorm(const uint8_t *tiles, const uint8_t *gate_tiles, const float *h,
+                                  const float *norm_weight, float eps, const float *add, float *y, int N, int K,
+                                  int B, int op, const q4rdna_cfg *cfg, void *workspace, size_t workspace_bytes,
+                                  q4rdna_stream_t stream) {
+    if (norm_weight == nullptr || !(eps >= 0.0f) || op < Q4RDNA_OP_PLAIN || op > Q4RDNA_OP_SWIGLU)
+        return Q4RDNA_ERR_INVALID_ARGUMENT;
+    return gemv_common(op, tiles, gate_tiles, h, add, y, N, K, B, cfg, workspace, workspace_bytes,
+                       (cudaStream_t)stream, norm_weight, eps);
+}
+
 q4rdna_status q4rdna_dequant_f32(const uint8_t *tiles, float *W, int N, int K, q4rdna_stream_t stream) {
     q4rdna_status st = check_shape(N, K, 1);
     if (st != Q4RDNA_OK) return st;
@@ -902,8 +961,9 @@ q4rdna_status q4rdna_plan_create(const q4rdna_gemv_desc *descs, int count, int B
         if (e.op == Q4RDNA_OP_ADD && e.add == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
         if (e.op == Q4RDNA_OP_SWIGLU && e.gate_tiles == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
         if (!aligned(e.tiles, 16) || (e.gate_tiles && !aligned(e.gate_tiles, 16)) || !aligned(e.x, 8) ||
-            !aligned(e.y, 4) || (e.add && !aligned(e.add, 4)))
+            !aligned(e.y, 4) || (e.add && !aligned(e.add, 4)) || (e.norm_weight && !aligned(e.norm_weight, 8)))
             return Q4RDNA_ERR_ALIGNMENT;
+        if (e.norm_weight != nullptr && !norm_supported(B)) return Q4RDNA_ERR_UNSUPPORTED;
         const int planes = e.op == Q4RDNA_OP_SWIGLU ? 2 : 1;
         const int G = e.K / Q4_GROUP;
         const int RB = (e.N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
@@ -922,9 +982,11 @@ q4rdna_status q4rdna_plan_create(const q4rdna_gemv_desc *descs, int count, int B
         T.part = nullptr; T.ticket = nullptr;
         T.N = e.N; T.K = e.K; T.G = G; T.RB = RB; T.S = sp.S; T.Gs = sp.Gs; T.op = e.op; T.nmirror = 0;
         T.item_begin = items;
+        T.gn = e.norm_weight;
+        T.eps = e.norm_eps;
         items += (long long)RB * sp.S;
         ws_off[i] = ws_total;
-        ws_total += plan_ws_bytes_for(e.N, B, sp.S, e.op);
+        ws_total += plan_ws_bytes_for(e.N, B, sp.S, e.op, e.norm_weight != nullptr);
         wbytes += (uint64_t)planes * Q4_TENSOR_BYTES(e.N, e.K);
         abytes += (uint64_t)planes * Q4_TENSOR_BYTES(e.N, e.K) + 4ull * e.K * B + 4ull * e.N * B +
                   (e.op == Q4RDNA_OP_ADD ? 4ull * e.N * B : 0ull);
@@ -940,6 +1002,9 @@ q4rdna_status q4rdna_plan_create(const q4rdna_gemv_desc *descs, int count, int B
             uint8_t *base = static_cast<uint8_t *>(p->workspace) + ws_off[i];
             T.ticket = reinterpret_cast<unsigned *>(base);
             T.part = reinterpret_cast<float *>(base + align256((size_t)T.RB * sizeof(unsigned)));
+            if (T.gn != nullptr)
+                T.nss = reinterpret_cast<float *>(base + align256((size_t)T.RB * sizeof(unsigned)) +
+                                                  align256(partial_bytes(T.N, B, T.S, T.op)));
         }
     }
     if (cudaMalloc(&p->table, sizeof(Task) * count) != cudaSuccess ||
@@ -950,6 +1015,7 @@ q4rdna_status q4rdna_plan_create(const q4rdna_gemv_desc *descs, int count, int B
     bool any_dual = false;
     for (int i = 0; i < count; ++i) any_dual = any_dual || descs[i].op == Q4RDNA_OP_SWIGLU;
     p->count = count; p->B = B; p->nb = B; p->items = items; p->dual = any_dual;
+    for (int i = 0; i < count; ++i) p->norm = p->norm || descs[i].norm_weight != nullptr;
     p->host = host;
     p->grid = grid_for(items, B, any_dual, d);
     p->ws_bytes = ws_total; p->weight_bytes = wbytes; p->algo_bytes = abytes;
@@ -977,7 +1043,7 @@ q4rdna_status q4rdna_plan_run(q4rdna_plan *plan, q4rdna_stream_t stream) {
         L.ntasks = plan->count;
         L.B = plan->B;
         L.total_items = plan->items;
-        return launch(L, plan->grid, plan->nb, plan->dual, (cudaStream_t)stream);
+        return launch(L, plan->grid, plan->nb, plan->dual, (cudaStream_t)stream, plan->norm);
     }
     const uint32_t epoch = plan->epoch + 1;
     q4rdna_status st;
@@ -989,7 +1055,7 @@ q4rdna_status q4rdna_plan_run(q4rdna_plan *plan, q4rdna_stream_t stream) {
         L.ntasks = plan->count;
         L.B = plan->B;
         L.total_items = plan->items;
-        st = launch(L, plan->grid, plan->nb, plan->dual, (cudaStream_t)stream);
+        st = launch(L, plan->grid, plan->nb, plan->dual, (cudaStream_t)stream, plan->norm);
     }
     if (st != Q4RDNA_OK) return st;
     GatherSignal sg = plan->sig;
@@ -1184,7 +1250,7 @@ q4rdna_status launch_segments(q4rdna_plan *plan, cudaStream_t cs, const uint8_t 
         L.ntasks = sg.count;
         L.B = plan->B;
         L.total_items = sg.items;
-        const q4rdna_status st = launch(L, sg.grid, plan->nb, plan->dual, c);
+        const q4rdna_status st = launch(L, sg.grid, plan->nb, plan->dual, c, plan->norm);
         if (st != Q4RDNA_OK) return st;
         if (cudaEventRecord(sg.y_ready, c) != cudaSuccess) return Q4RDNA_ERR_CUDA;
         if (!copies) continue;

@@ -36,11 +36,29 @@ template <int BB>
 struct __align__(16) I8X {
     uint32_t xq[BB][Q4_GROUP];  // per k: the integer X (bytes B0, B1, B2 used)
     float up[BB];               // 2^e: undoes the group's power-of-two scaling
+    float ss[BB];               // fused RMSNorm: the group's sum of h^2
 };
 
 // Branch-free, so that the compiler can interleave it with the previous
 // group's MMAs (see run_item_i8).
-__device__ __forceinline__ void prep_group_i8(float2 v, uint32_t *xq_row, float *up, int lane) {
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// NORM kernels, norm: v is the raw RMSNorm input h, gv the norm weight of the
+// same columns; the group is then prepared as h * g, and its sum of h^2 goes to
+// *ss.  Without NORM the function stays branch-free.
+template <bool NORM>
+__device__ __forceinline__ void prep_group_i8(float2 v, float2 gv, bool norm, uint32_t *xq_row, float *up,
+                                              float *ss, int lane) {
+    if (NORM && norm) {
+        const float q = warp_sum(fmaf(v.x, v.x, v.y * v.y));
+        if (lane == 0) *ss = q;
+        v.x *= gv.x;
+        v.y *= gv.y;
+    }
     const float m = warp_max(fmaxf(fabsf(v.x), fabsf(v.y)));
     // biased exponent E of the max: scale by 2^(148 - E) so max*scale < 2^22.
     // E >= 22 keeps both 2^(148 - E) and 2^(E - 148) normal f32 numbers; only
@@ -228,9 +246,11 @@ __device__ __forceinline__ void mma_step_i8(Src &src, const I8X<BB> &sm, float (
 }
 
 // Epilogue of one item in the int8 layout: lane rows tile_row*32 + 16h + c + 4q.
-template <int BB, bool DUAL>
+// iss: fused RMSNorm (NORM kernels), the item's sum of h^2 per batch column.
+template <int BB, bool DUAL, bool NORM>
 __device__ __forceinline__ void finish_rows_i8(const Task &T, int rb, int s, int B, float (&acc)[2][4][BB],
-                                               int lane, bool valid, int tile_row, int h, int c) {
+                                               const float (&iss)[BB], int lane, bool valid, int tile_row, int h,
+                                               int c) {
     const int row0 = tile_row * Q4_TILE_ROWS + 16 * h + c;
     if (T.S == 1) {
         if (valid) {
@@ -240,12 +260,23 @@ __device__ __forceinline__ void finish_rows_i8(const Task &T, int rb, int s, int
                 for (int b = 0; b < BB; ++b) {
                     if (b >= B) continue;
                     const size_t idx = (size_t)b * T.N + row0 + 4 * q;
-                    put_y(T, idx, finish(acc[0][q][b], acc[DUAL ? 1 : 0][q][b], T.op, T.add, idx));
+                    float v = acc[0][q][b], gate = acc[DUAL ? 1 : 0][q][b];
+                    if (NORM && T.gn != nullptr) {
+                        const float r = norm_scale(T, iss[b]);
+                        v *= r;
+                        gate *= r;
+                    }
+                    put_y(T, idx, finish(v, gate, T.op, T.add, idx));
                 }
         }
         return;
     }
     constexpr int planes = DUAL ? 2 : 1;
+    if (NORM && T.gn != nullptr && lane == 0) {
+#pragma unroll
+        for (int b = 0; b < BB; ++b)
+            if (b < B) __stcg(&T.nss[((size_t)rb * T.S + s) * B + b], iss[b]);
+    }
     if (valid) {
 #pragma unroll
         for (int pl = 0; pl < planes; ++pl)
@@ -263,7 +294,7 @@ __device__ __forceinline__ void finish_rows_i8(const Task &T, int rb, int s, int
     if (lane == 0) prev = atomicAdd(&T.ticket[rb], 1u);
     prev = __shfl_sync(0xffffffffu, prev, 0);
     if (prev != (unsigned)(T.S - 1)) return;
-    reduce_splits<DUAL>(T, rb, B, lane);
+    reduce_splits<DUAL, NORM>(T, rb, B, lane);
 }
 
 // This lane's tile of step 0 of an item, and the item's first group.  Rows past
@@ -286,6 +317,7 @@ struct XCursor {
     long long it;      // item (>= total: past the warp's last group)
     int g, ng, g0, K;  // group within the item, the item's groups, first group, columns
     const float *x;
+    const float *gn;   // fused RMSNorm weight, or null
 };
 
 __device__ __forceinline__ void xc_load(const Launch &L, XCursor &c) {
@@ -297,6 +329,7 @@ __device__ __forceinline__ void xc_load(const Launch &L, XCursor &c) {
     c.g = 0;
     c.K = T.K;
     c.x = T.x;
+    c.gn = T.gn;
 }
 
 __device__ __forceinline__ void xc_advance(const Launch &L, XCursor &c, long long nw) {
@@ -307,14 +340,19 @@ __device__ __forceinline__ void xc_advance(const Launch &L, XCursor &c, long lon
     }
 }
 
-template <int BB>
-__device__ __forceinline__ void xc_fetch(const Launch &L, const XCursor &c, int lane, float2 (&xv)[BB]) {
+template <int BB, bool NORM>
+__device__ __forceinline__ void xc_fetch(const Launch &L, const XCursor &c, int lane, float2 (&xv)[BB], float2 &gv,
+                                         bool &norm) {
     if (c.it >= L.total_items) return;
 #pragma unroll
     for (int b = 0; b < BB; ++b)
         if (b < L.B)
             xv[b] = __ldg(reinterpret_cast<const float2 *>(c.x + (size_t)b * c.K + (size_t)(c.g0 + c.g) * Q4_GROUP) +
                           lane);
+    if (NORM) {
+        norm = c.gn != nullptr;
+        if (norm) gv = __ldg(reinterpret_cast<const float2 *>(c.gn + (size_t)(c.g0 + c.g) * Q4_GROUP) + lane);
+    }
 }
 
 // Per-warp state carried from item to item.
@@ -322,19 +360,21 @@ template <int BB>
 struct I8Pipe {
     StepBufI8 buf;   // code and scale words of the next step (register pipeline)
     float2 xv[BB];   // raw x of the next group to prepare
+    float2 gv;       // fused RMSNorm: the norm weight of that group's columns
+    bool norm;       // that group belongs to a fused-RMSNorm task
     XCursor xc;      // the group whose raw x is in xv
     int par;         // activation buffer holding the group being multiplied
 };
 
 // Prepare the raw x in P.xv (the cursor's group) into activation buffer xs;
 // past the warp's last group it writes a spare buffer that is never read.
-template <int BB>
+template <int BB, bool NORM>
 __device__ __forceinline__ void prep_ahead(I8Pipe<BB> &P, I8X<BB> &xs, int lane) {
 #pragma unroll
-    for (int b = 0; b < BB; ++b) prep_group_i8(P.xv[b], xs.xq[b], &xs.up[b], lane);
+    for (int b = 0; b < BB; ++b) prep_group_i8<NORM>(P.xv[b], P.gv, P.norm, xs.xq[b], &xs.up[b], &xs.ss[b], lane);
 }
 
-template <int BB, bool DUAL>
+template <int BB, bool DUAL, bool NORM>
 __device__ __forceinline__ void run_item_i8(const Launch &L, const Task &T, int local, I8X<BB> (&xs)[2], int lane,
                                             const I8Sel &sel, I8Pipe<BB> &P, const Task *nT, int nlocal,
                                             long long nw) {
@@ -357,6 +397,10 @@ __device__ __forceinline__ void run_item_i8(const Launch &L, const Task &T, int 
         for (int q = 0; q < 4; ++q)
 #pragma unroll
             for (int b = 0; b < BB; ++b) acc[pl][q][b] = 0.0f;
+    float iss[BB];
+#pragma unroll
+    for (int b = 0; b < BB; ++b) iss[b] = 0.0f;
+    const bool norm = NORM && T.gn != nullptr;
 
     for (int st = 0; st < nsteps; ++st) {
         const int tt = DUAL ? (st & 1) : 0;
@@ -371,10 +415,14 @@ __device__ __forceinline__ void run_item_i8(const Launch &L, const Task &T, int 
         I8X<BB> &cur = xs[P.par];
         if (tt == 0) {
             mma_step_i8<BB>(src, cur, acc[0], lane, sel);
+            if (norm) {
+#pragma unroll
+                for (int b = 0; b < BB; ++b) iss[b] += cur.ss[b];  // groups in ascending order
+            }
             // The next group's activation goes into the other buffer while the
             // MMAs above drain: no branch in between, so the compiler can
             // interleave the two independent chains.
-            prep_ahead<BB>(P, xs[P.par ^ 1], lane);
+            prep_ahead<BB, NORM>(P, xs[P.par ^ 1], lane);
         } else {
             mma_step_i8<BB>(src, cur, acc[1], lane, sel);
         }
@@ -384,18 +432,19 @@ __device__ __forceinline__ void run_item_i8(const Launch &L, const Task &T, int 
             __syncwarp();
             P.par ^= 1;
             xc_advance(L, P.xc, nw);
-            xc_fetch<BB>(L, P.xc, lane, P.xv);
+            xc_fetch<BB, NORM>(L, P.xc, lane, P.xv, P.gv, P.norm);
         }
     }
     if (DUAL)
-        finish_rows_i8<BB, true>(T, rb, s, L.B, acc, lane, valid, tile_row, h, c);
+        finish_rows_i8<BB, true, NORM>(T, rb, s, L.B, acc, iss, lane, valid, tile_row, h, c);
     else
-        finish_rows_i8<BB, false>(T, rb, s, L.B, acc, lane, valid, tile_row, h, c);
+        finish_rows_i8<BB, false, NORM>(T, rb, s, L.B, acc, iss, lane, valid, tile_row, h, c);
 }
 
 // HAS_DUAL = false: the launch holds no SwiGLU task, so the SwiGLU path (and its
 // registers) is compiled out.
-template <int BB, bool HAS_DUAL>
+// NORM = false: the launch holds no fused-RMSNorm task, so that path is compiled out.
+template <int BB, bool HAS_DUAL, bool NORM>
 __global__ void __launch_bounds__(kThreads, BB <= 2 ? 2 : 1) q4_gemv_i8_kernel(const __grid_constant__ Launch L) {
     __shared__ I8X<BB> xsm[kWarps][2];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -419,13 +468,15 @@ __global__ void __launch_bounds__(kThreads, BB <= 2 ? 2 : 1) q4_gemv_i8_kernel(c
     }
 #pragma unroll
     for (int b = 0; b < BB; ++b) P.xv[b] = make_float2(0.0f, 0.0f);
+    P.gv = make_float2(0.0f, 0.0f);
+    P.norm = false;
     // the warp's first group into buffer 0, the second group's raw x in flight
     P.xc.it = it;
     xc_load(L, P.xc);
-    xc_fetch<BB>(L, P.xc, lane, P.xv);
-    prep_ahead<BB>(P, xs[0], lane);
+    xc_fetch<BB, NORM>(L, P.xc, lane, P.xv, P.gv, P.norm);
+    prep_ahead<BB, NORM>(P, xs[0], lane);
     xc_advance(L, P.xc, nw);
-    xc_fetch<BB>(L, P.xc, lane, P.xv);
+    xc_fetch<BB, NORM>(L, P.xc, lane, P.xv, P.gv, P.norm);
     __syncwarp();
     for (; it < L.total_items; it += nw) {
         const Task &T = find_task(L, it);
@@ -433,8 +484,8 @@ __global__ void __launch_bounds__(kThreads, BB <= 2 ? 2 : 1) q4_gemv_i8_kernel(c
         const Task *nT = nit < L.total_items ? &find_task(L, nit) : nullptr;
         const int nlocal = nT ? (int)(nit - nT->item_begin) : 0;
         if (HAS_DUAL && T.op == Q4RDNA_OP_SWIGLU)
-            run_item_i8<BB, true>(L, T, (int)(it - T.item_begin), xs, lane, sel, P, nT, nlocal, nw);
+            run_item_i8<BB, true, NORM>(L, T, (int)(it - T.item_begin), xs, lane, sel, P, nT, nlocal, nw);
         else
-            run_item_i8<BB, false>(L, T, (int)(it - T.item_begin), xs, lane, sel, P, nT, nlocal, nw);
+            run_item_i8<BB, false, NORM>(L, T, (int)(it - T.item_begin), xs, lane, sel, P, nT, nlocal, nw);
     }
 }

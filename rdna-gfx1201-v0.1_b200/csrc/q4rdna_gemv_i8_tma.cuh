@@ -58,6 +58,10 @@ __device__ __forceinline__ void producer_issue(const I8Producer &p, uint32_t sta
     }
 }
 
+// The ring variant takes no fused-RMSNorm task (the host refuses them).
+template <int BB>
+__device__ const float kNoSumsq[BB] = {};
+
 // 70 KB per CTA, 3 CTAs (24 warps) per SM, one group in flight per warp: the
 // fastest ring shape measured on B200 (the register kernel is faster still).
 using I8Ring = RingCfg<2, 1, 8, 3>;
@@ -160,7 +164,9 @@ __global__ void __launch_bounds__(R::THREADS, R::MINB) q4_gemv_i8_tma_kernel(con
                     __syncwarp();
 #pragma unroll
                     for (int b = 0; b < BB; ++b)
-                        if (b < L.B) prep_group_i8(xv[b], sm.xq[b], &sm.up[b], lane);
+                        if (b < L.B)
+                            prep_group_i8<false>(xv[b], make_float2(0.0f, 0.0f), false, sm.xq[b], &sm.up[b], &sm.ss[b],
+                                                 lane);
 #pragma unroll
                     for (int b = 0; b < BB; ++b) {
                         if (b >= L.B) continue;
@@ -187,9 +193,9 @@ __global__ void __launch_bounds__(R::THREADS, R::MINB) q4_gemv_i8_tma_kernel(con
         }
         if (fault) break;
         if (dual)
-            finish_rows_i8<BB, true>(T, rb, s, L.B, acc, lane, valid, tile_row, h, c);
+            finish_rows_i8<BB, true, false>(T, rb, s, L.B, acc, kNoSumsq<BB>, lane, valid, tile_row, h, c);
         else
-            finish_rows_i8<BB, false>(T, rb, s, L.B, acc, lane, valid, tile_row, h, c);
+            finish_rows_i8<BB, false, false>(T, rb, s, L.B, acc, kNoSumsq<BB>, lane, valid, tile_row, h, c);
     }
     if (fault) {
         if (lane == 0) atomicOr(&g_fault, kFaultWaitTimeout);

@@ -52,6 +52,7 @@ template <int BP>
 struct __align__(16) MbSmem {
     uint2 b[2][4][MbShape<BP>::NT][2][32];  // [buffer][group][n-tile][k-step][lane]: b0, b1
     float up[2][4][BP];                     // 2^e per (group, batch column)
+    float ss[2][4][BP];                     // fused RMSNorm: sum of h^2 per (group, batch column)
     unsigned last;                          // split ticket of this CTA's item
 };
 
@@ -201,7 +202,7 @@ __device__ __forceinline__ void mb_prefetch_x(const MbCursor &c, int B, int tid)
 }
 
 // The CTA prepares the B fragments of chunk c into buffer `par`.
-template <int BP>
+template <int BP, bool NORM>
 __device__ __forceinline__ void mb_prep(MbSmem<BP> &sm, int par, const MbCursor &c, int B, int tid) {
     using S = MbShape<BP>;
     constexpr int PER = 8 * BP;
@@ -216,6 +217,23 @@ __device__ __forceinline__ void mb_prep(MbSmem<BP> &sm, int par, const MbCursor 
 #pragma unroll
         for (int j = 0; j < 4; ++j)
             v[j] = live ? __ldg(reinterpret_cast<const float2 *>(xp + 8 * j)) : make_float2(0.0f, 0.0f);
+        if (NORM && c.T->gn != nullptr) {
+            // fused RMSNorm: v is the raw input h; the group is prepared as h * g
+            const float *gp = c.T->gn + (xp - (c.T->x + (size_t)(live ? b : 0) * c.T->K));
+            float q = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                q = fmaf(v[j].x, v[j].x, q);
+                q = fmaf(v[j].y, v[j].y, q);
+                const float2 g = live ? __ldg(reinterpret_cast<const float2 *>(gp + 8 * j)) : make_float2(0.0f, 0.0f);
+                v[j].x *= g.x;
+                v[j].y *= g.y;
+            }
+            q += __shfl_xor_sync(0xffffffffu, q, 1);
+            q += __shfl_xor_sync(0xffffffffu, q, 2);
+            q += __shfl_xor_sync(0xffffffffu, q, 4);
+            if (gi < c.ncg && (r & 7) == 0) sm.ss[par][gi][b] = q;
+        }
         float m = 0.0f;
 #pragma unroll
         for (int j = 0; j < 4; ++j) m = fmaxf(m, fmaxf(fabsf(v[j].x), fabsf(v[j].y)));
@@ -312,12 +330,16 @@ __device__ __forceinline__ void mb_tile(const MbTileRegs &r, const MbSmem<BP> &s
 
 // Item epilogue: store (S == 1), or write this warp's split partials and, in the
 // CTA that arrives last at row block rb, add the splits in ascending order.
-template <int BP, bool HAS_DUAL>
+// iss: fused RMSNorm (NORM kernels), the item's sum of h^2 per (batch block,
+// column) of this lane.
+template <int BP, bool HAS_DUAL, bool NORM>
 __device__ __forceinline__ void mb_finish(const Task &T, int rb, int s, int B, float (&acc)[HAS_DUAL ? 2 : 1][4][BP / 8][2],
-                                          bool dual, bool valid, int tile_row, int lane, int tid, MbSmem<BP> &sm) {
+                                          const float (&iss)[BP / 8][2], bool dual, bool valid, int tile_row,
+                                          int lane, int tid, MbSmem<BP> &sm) {
     using S = MbShape<BP>;
     const int g = lane >> 2, c = lane & 3;
     const int row0 = tile_row * Q4_TILE_ROWS + 4 * g;
+    const bool norm = NORM && T.gn != nullptr;
     if (T.S == 1) {
         if (valid) {
 #pragma unroll
@@ -329,13 +351,28 @@ __device__ __forceinline__ void mb_finish(const Task &T, int rb, int s, int B, f
                         const int b = 8 * bb + 2 * c + q;
                         if (b >= B) continue;
                         const size_t idx = (size_t)b * T.N + row0 + r;
-                        const float gate = HAS_DUAL ? acc[HAS_DUAL ? 1 : 0][r][bb][q] : 0.0f;
-                        put_y(T, idx, finish(acc[0][r][bb][q], dual ? gate : 0.0f, T.op, T.add, idx));
+                        float v = acc[0][r][bb][q];
+                        float gate = HAS_DUAL ? acc[HAS_DUAL ? 1 : 0][r][bb][q] : 0.0f;
+                        if (NORM && norm) {
+                            const float nr = norm_scale(T, iss[bb][q]);
+                            v *= nr;
+                            gate *= nr;
+                        }
+                        put_y(T, idx, finish(v, dual ? gate : 0.0f, T.op, T.add, idx));
                     }
         }
         return;
     }
     const int planes = dual ? 2 : 1;
+    if (NORM && norm && tid < 4) {  // warp 0, lanes g = 0: every batch column once
+#pragma unroll
+        for (int bb = 0; bb < S::NBB; ++bb)
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int b = 8 * bb + 2 * c + q;
+                if (b < B) __stcg(&T.nss[((size_t)rb * T.S + s) * B + b], iss[bb][q]);
+            }
+    }
     if (valid) {
 #pragma unroll
         for (int pl = 0; pl < (HAS_DUAL ? 2 : 1); ++pl) {
@@ -368,6 +405,11 @@ __device__ __forceinline__ void mb_finish(const Task &T, int rb, int s, int B, f
                 s0 += __ldcg(p0 + sp * split_stride);
                 if (dual) s1 += __ldcg(p0 + sp * split_stride + (size_t)B * T.N);
             }
+            if (NORM && norm) {
+                const float nr = norm_scale(T, split_sumsq(T, rb, b, B));
+                s0 *= nr;
+                s1 *= nr;
+            }
             const size_t idx = (size_t)b * T.N + row;
             put_y(T, idx, finish(s0, s1, T.op, T.add, idx));
         }
@@ -381,7 +423,8 @@ __device__ __forceinline__ void mb_finish(const Task &T, int rb, int s, int B, f
 // and refills every slot with the next chunk's tile as soon as it is consumed;
 // then the CTA prepares the next chunk's activation fragments (prefetched into
 // L1 one chunk earlier) into the other buffer and meets once.
-template <int BP, bool HAS_DUAL>
+// NORM = false: the launch holds no fused-RMSNorm task, so that path is compiled out.
+template <int BP, bool HAS_DUAL, bool NORM>
 __global__ void __launch_bounds__(kMbThreads, BP <= 8 ? 4 : 3) q4_gemv_mb_kernel(const __grid_constant__ Launch L) {
     using S = MbShape<BP>;
     __shared__ MbSmem<BP> sm;
@@ -398,7 +441,7 @@ __global__ void __launch_bounds__(kMbThreads, BP <= 8 ? 4 : 3) q4_gemv_mb_kernel
         for (int sl = 0; sl < S::SLOTS; ++sl)
             if (sl < ns) mb_load_tile(tr[sl], mb_tile_addr(cur, sl, warp), g, c);
     }
-    mb_prep<BP>(sm, 0, cur, L.B, tid);
+    mb_prep<BP, NORM>(sm, 0, cur, L.B, tid);
     __syncthreads();
     MbCursor nxt = cur;
     mb_advance<HAS_DUAL>(L, nxt, stride);
@@ -406,12 +449,15 @@ __global__ void __launch_bounds__(kMbThreads, BP <= 8 ? 4 : 3) q4_gemv_mb_kernel
     int par = 0;
 
     float acc[HAS_DUAL ? 2 : 1][4][S::NBB][2];
+    float iss[S::NBB][2];
 #pragma unroll
     for (int pl = 0; pl < (HAS_DUAL ? 2 : 1); ++pl)
 #pragma unroll
         for (int r = 0; r < 4; ++r)
 #pragma unroll
             for (int bb = 0; bb < S::NBB; ++bb) acc[pl][r][bb][0] = acc[pl][r][bb][1] = 0.0f;
+#pragma unroll
+    for (int bb = 0; bb < S::NBB; ++bb) iss[bb][0] = iss[bb][1] = 0.0f;
 
     while (true) {
         const bool more = nxt.it < L.total_items;
@@ -420,26 +466,36 @@ __global__ void __launch_bounds__(kMbThreads, BP <= 8 ? 4 : 3) q4_gemv_mb_kernel
         for (int sl = 0; sl < S::SLOTS; ++sl) {
             if (sl < ns) {
                 const int gi = cur.dual ? (sl >> 1) : sl;
-                if (HAS_DUAL && cur.dual && (sl & 1))
+                if (HAS_DUAL && cur.dual && (sl & 1)) {
                     mb_tile<BP>(tr[sl], sm, par, gi, lane, acc[HAS_DUAL ? 1 : 0]);
-                else
+                } else {
                     mb_tile<BP>(tr[sl], sm, par, gi, lane, acc[0]);
+                    if (NORM && cur.T->gn != nullptr) {  // fused RMSNorm: groups in ascending order
+#pragma unroll
+                        for (int bb = 0; bb < S::NBB; ++bb) {
+                            iss[bb][0] += sm.ss[par][gi][8 * bb + 2 * c];
+                            iss[bb][1] += sm.ss[par][gi][8 * bb + 2 * c + 1];
+                        }
+                    }
+                }
             }
             if (sl < nns) mb_load_tile(tr[sl], mb_tile_addr(nxt, sl, warp), g, c);
         }
         if (mb_last_chunk(cur)) {
             const int tile_row = cur.rb * Q4_BLOCK_TILES + warp;
             const bool valid = tile_row < (cur.T->N >> 5);
-            mb_finish<BP, HAS_DUAL>(*cur.T, cur.rb, cur.s, L.B, acc, cur.dual, valid, tile_row, lane, tid, sm);
+            mb_finish<BP, HAS_DUAL, NORM>(*cur.T, cur.rb, cur.s, L.B, acc, iss, cur.dual, valid, tile_row, lane, tid, sm);
 #pragma unroll
             for (int pl = 0; pl < (HAS_DUAL ? 2 : 1); ++pl)
 #pragma unroll
                 for (int r = 0; r < 4; ++r)
 #pragma unroll
                     for (int bb = 0; bb < S::NBB; ++bb) acc[pl][r][bb][0] = acc[pl][r][bb][1] = 0.0f;
+#pragma unroll
+            for (int bb = 0; bb < S::NBB; ++bb) iss[bb][0] = iss[bb][1] = 0.0f;
         }
         if (!more) break;
-        mb_prep<BP>(sm, par ^ 1, nxt, L.B, tid);
+        mb_prep<BP, NORM>(sm, par ^ 1, nxt, L.B, tid);
         __syncthreads();
         par ^= 1;
         cur = nxt;

@@ -41,7 +41,8 @@ class Cfg(ctypes.Structure):
 
 class GemvDesc(ctypes.Structure):
     _fields_ = [("tiles", c_void_p), ("gate_tiles", c_void_p), ("x", c_void_p), ("add", c_void_p),
-                ("y", c_void_p), ("N", c_int), ("K", c_int), ("op", c_int), ("split", c_int)]
+                ("y", c_void_p), ("N", c_int), ("K", c_int), ("op", c_int), ("split", c_int),
+                ("norm_weight", c_void_p), ("norm_eps", ctypes.c_float)]
 
 
 class PlanInfo(ctypes.Structure):
@@ -61,6 +62,8 @@ def _bind(lib):
         "q4rdna_gemv_add": (c_int, [P, P, P, P, c_int, c_int, c_int, POINTER(Cfg), P, c_size_t, P]),
         "q4rdna_gemv_swiglu": (c_int, [P, P, P, P, c_int, c_int, c_int, POINTER(Cfg), P, c_size_t, P]),
         "q4rdna_dequant_f32": (c_int, [P, P, c_int, c_int, P]),
+        "q4rdna_gemv_rmsnorm": (c_int, [P, P, P, P, ctypes.c_float, P, P, c_int, c_int, c_int, c_int, POINTER(Cfg), P,
+                                        c_size_t, P]),
         "q4rdna_pack_bf16": (c_int, [P, P, c_int, c_int, P]),
         "q4rdna_gemv_noalloc": (c_int, [P, P, P, c_int, c_int, c_int, POINTER(Cfg), P]),
         "q4rdna_plan_create": (c_int, [POINTER(GemvDesc), c_int, c_int, POINTER(P)]),
@@ -101,6 +104,7 @@ lib = _bind(ctypes.CDLL(LIB_PATH)) if os.path.exists(LIB_PATH) else None
 SYMBOLS = [
     "q4rdna_status_string", "q4rdna_version", "q4rdna_select_split", "q4rdna_workspace_bytes",
     "q4rdna_workspace_init", "q4rdna_gemv", "q4rdna_gemv_add", "q4rdna_gemv_swiglu", "q4rdna_dequant_f32", "q4rdna_pack_bf16",
+    "q4rdna_gemv_rmsnorm",
     "q4rdna_gemv_noalloc",
     "q4rdna_plan_create", "q4rdna_plan_run", "q4rdna_plan_get_info", "q4rdna_plan_destroy",
     "q4rdna_plan_run_host", "q4rdna_plan_set_segments", "q4rdna_plan_set_gather", "q4rdna_plan_gather_parity", "q4rdna_ipc_alloc", "q4rdna_ipc_open",
@@ -186,11 +190,14 @@ def _rows(tiles, K: int) -> int:
     return n // (34 * K)
 
 
-def gemv(tiles, x, *, op: int = OP_PLAIN, add=None, gate_tiles=None, out=None, split: int = 0, stream=None):
+def gemv(tiles, x, *, op: int = OP_PLAIN, add=None, gate_tiles=None, out=None, split: int = 0, stream=None,
+         norm_weight=None, norm_eps: float = 1e-6):
     """y = W x (op PLAIN), W x + add (ADD) or (W x) * silu(W_gate x) (SWIGLU).
 
     tiles / gate_tiles: uint8 CUDA tensors in the packed layout; x: f32 [B, K]
-    or [K]; add: f32 [B, N].  Returns f32 [B, N] (or [N]).
+    or [K]; add: f32 [B, N].  Returns f32 [B, N] (or [N]).  With norm_weight
+    (f32 [K]) x is the raw hidden state h and the GEMV input is
+    RMSNorm(h) * norm_weight, fused (q4rdna_gemv_rmsnorm).
     """
     import torch
 
@@ -204,7 +211,12 @@ def gemv(tiles, x, *, op: int = OP_PLAIN, add=None, gate_tiles=None, out=None, s
     nbytes = workspace_bytes(N, K, B, op, split)
     ws, wsn = _workspace(nbytes, x.device, st)
     L = _lib()
-    if op == OP_PLAIN:
+    if norm_weight is not None:
+        rc = L.q4rdna_gemv_rmsnorm(tiles.data_ptr(), gate_tiles.data_ptr() if gate_tiles is not None else None,
+                                   x2.data_ptr(), norm_weight.data_ptr(), norm_eps,
+                                   add.data_ptr() if add is not None else None, out.data_ptr(), N, K, B, op,
+                                   _cfg(split), ws, wsn, st)
+    elif op == OP_PLAIN:
         rc = L.q4rdna_gemv(tiles.data_ptr(), x2.data_ptr(), out.data_ptr(), N, K, B, _cfg(split), ws, wsn, st)
     elif op == OP_ADD:
         rc = L.q4rdna_gemv_add(tiles.data_ptr(), x2.data_ptr(), add.data_ptr(), out.data_ptr(), N, K, B,
@@ -261,7 +273,8 @@ class Plan:
     """Many independent GEMVs in one persistent launch (q4rdna_plan_*).
 
     ``descs``: list of dicts with keys tiles, x, y (torch CUDA tensors) and
-    optional op, add, gate_tiles, split.  The tensors must stay alive; x may
+    optional op, add, gate_tiles, split, norm_weight, norm_eps (fused RMSNorm:
+    x is then the raw hidden state).  The tensors must stay alive; x may
     be rewritten in place between runs.
     """
 
@@ -279,6 +292,8 @@ class Plan:
             arr[i].K = K
             arr[i].op = d.get("op", OP_PLAIN)
             arr[i].split = d.get("split", 0)
+            arr[i].norm_weight = d["norm_weight"].data_ptr() if d.get("norm_weight") is not None else None
+            arr[i].norm_eps = d.get("norm_eps", 1e-6)
         h = c_void_p()
         check(_lib().q4rdna_plan_create(arr, len(descs), B, ctypes.byref(h)), "plan_create")
         self._h = h
