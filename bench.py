@@ -254,7 +254,8 @@ def run_pack(args):
             "cpu_baseline": cpu, "gpu_launches": q4rdna.launch_count() - l0, "clocks": clk.summary()}
 
 
-def build_step(model: str, rank: int, world: int, device, seed: int, layers: int = 0, B: int = 1):
+def build_step(model: str, rank: int, world: int, device, seed: int, layers: int = 0, B: int = 1,
+               norm: bool = False):
     """Weights (this rank's row shard of every tensor), activations and outputs
     of one decode step, laid out by q4rdna.tp.Layout so that a step's inputs and
     outputs are each one contiguous buffer (one copy each way for the
@@ -282,7 +283,11 @@ def build_step(model: str, rank: int, world: int, device, seed: int, layers: int
         # each rank draws its own shard (same distributions; the shard of one
         # full tensor is a byte slice, q4rdna.tp.shard_tiles)
         t = synth.tiles_torch(s.rows, s.K, seed + 1 + i * world + rank, device)
-        descs.append({"tiles": t, "x": x_all[B * xo:B * (xo + s.K)].view(B, s.K), "y": lay.local_view(y_all, i)})
+        d = {"tiles": t, "x": x_all[B * xo:B * (xo + s.K)].view(B, s.K), "y": lay.local_view(y_all, i)}
+        if norm:  # x is the raw hidden state; the plan normalises it on the fly
+            d["norm_weight"] = torch.ones(s.K, dtype=torch.float32, device=device)
+            d["norm_eps"] = 1e-6
+        descs.append(d)
         xo += s.K
         wbytes += s.rows * s.K * 34 // 64
         abytes += s.rows * s.K * 34 // 64 + 4 * B * (s.K + s.rows)
@@ -312,7 +317,7 @@ def run_ours(args):
 
     B = args.batch
     descs, x_all, y_all, wbytes, abytes, ntensors, lay = build_step(args.model, rank, world, dev, args.seed,
-                                                                   args.layers, B)
+                                                                   args.layers, B, args.norm)
     plan = q4rdna.Plan(descs, B=B)
     plan.set_segments(args.run_segments)
     info = plan.info()
@@ -408,7 +413,7 @@ def run_ours(args):
                                    + (f" (first {args.layers} layers only)" if args.layers else "")
                                    + (f", rows sharded over {world} GPUs + " + ("all-gather fused into the plan kernel (P2P stores)"
                                       if p2p else "NCCL all-gather") if world > 1 else ""),
-                       "tensors": ntensors, "batch": B, "flops_per_step": 2 * B * wbytes * world * 64 // 34,
+                       "tensors": ntensors, "batch": B, "fused_rmsnorm": bool(args.norm), "flops_per_step": 2 * B * wbytes * world * 64 // 34,
                        "weight_bytes_per_step": wbytes * world,
                        "algo_bytes_per_step": total_algo, "parallelism": f"tp{world}" if world > 1 else "none",
                        "l2": f"no flush: {wbytes * world / 1e9:.2f} GB streamed per step >> 126 MB L2",
@@ -471,6 +476,8 @@ def main():
                     help="N > 1: all-gather fused into the plan kernel (p2p) or one NCCL all-gather per step")
     ap.add_argument("--pack", action="store_true",
                     help="time the GPU sidecar packer on the model's weights instead of the GEMV step")
+    ap.add_argument("--norm", action="store_true",
+                    help="every GEMV takes the raw hidden state and applies RMSNorm in the kernel (fused producer)")
     ap.add_argument("--run-segments", type=int, default=0,
                     help="device-resident step as this many overlapping launches (0: library default, 1: one launch)")
     ap.add_argument("--segments", type=int, default=0,

@@ -289,6 +289,9 @@ template <bool DUAL, bool NORM = false>
 __device__ __forceinline__ void reduce_splits(const Task &T, int rb, int B, int lane) {
     constexpr int planes = DUAL ? 2 : 1;
     __threadfence();
+    // fused RMSNorm: lane b computes batch column b's scale once (B <= 16)
+    float nr_lane = 1.0f;
+    if (NORM && T.gn != nullptr && lane < B) nr_lane = norm_scale(T, split_sumsq(T, rb, lane, B));
     for (int q4r = 0; q4r < Q4_BLOCK_TILES; ++q4r) {
         const int row = rb * Q4_BLOCK_ROWS + 32 * q4r + lane;
         if (row >= T.N) break;
@@ -302,7 +305,7 @@ __device__ __forceinline__ void reduce_splits(const Task &T, int rb, int B, int 
                 if (DUAL) s1 += __ldcg(p0 + sp * split_stride + (size_t)B * T.N);
             }
             if (NORM && T.gn != nullptr) {
-                const float r = norm_scale(T, split_sumsq(T, rb, b, B));
+                const float r = __shfl_sync(0xffffffffu, nr_lane, b);
                 s0 *= r;
                 s1 *= r;
             }

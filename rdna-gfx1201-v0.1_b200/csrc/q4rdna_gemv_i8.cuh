@@ -47,19 +47,30 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-// NORM kernels, norm: v is the raw RMSNorm input h, gv the norm weight of the
-// same columns; the group is then prepared as h * g, and its sum of h^2 goes to
-// *ss.  Without NORM the function stays branch-free.
+// NORM kernels: v is the raw RMSNorm input h and gv the norm weight of the same
+// columns (1 for the launch's tasks without a norm); the group is prepared as
+// h * g and its sum of h^2 goes to *ss.  Branch-free either way, so that the
+// compiler can interleave it with the previous group's MMAs.
 template <bool NORM>
 __device__ __forceinline__ void prep_group_i8(float2 v, float2 gv, bool norm, uint32_t *xq_row, float *up,
                                               float *ss, int lane) {
-    if (NORM && norm) {
-        const float q = warp_sum(fmaf(v.x, v.x, v.y * v.y));
-        if (lane == 0) *ss = q;
+    (void)norm;
+    float m;
+    if (NORM) {
+        // the sum of h^2 and the max of |h * g| share the shuffle rounds
+        float q = fmaf(v.x, v.x, v.y * v.y);
         v.x *= gv.x;
         v.y *= gv.y;
+        m = fmaxf(fabsf(v.x), fabsf(v.y));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            q += __shfl_xor_sync(0xffffffffu, q, o);
+        }
+        if (lane == 0) *ss = q;
+    } else {
+        m = warp_max(fmaxf(fabsf(v.x), fabsf(v.y)));
     }
-    const float m = warp_max(fmaxf(fabsf(v.x), fabsf(v.y)));
     // biased exponent E of the max: scale by 2^(148 - E) so max*scale < 2^22.
     // E >= 22 keeps both 2^(148 - E) and 2^(E - 148) normal f32 numbers; only
     // groups whose largest |x| is below 2^-104 lose bits to the clamp.
@@ -262,7 +273,7 @@ __device__ __forceinline__ void finish_rows_i8(const Task &T, int rb, int s, int
                     const size_t idx = (size_t)b * T.N + row0 + 4 * q;
                     float v = acc[0][q][b], gate = acc[DUAL ? 1 : 0][q][b];
                     if (NORM && T.gn != nullptr) {
-                        const float r = norm_scale(T, iss[b]);
+                        const float r = norm_scale(T, iss[b]);  // the compiler hoists it out of q
                         v *= r;
                         gate *= r;
                     }
@@ -350,8 +361,11 @@ __device__ __forceinline__ void xc_fetch(const Launch &L, const XCursor &c, int 
             xv[b] = __ldg(reinterpret_cast<const float2 *>(c.x + (size_t)b * c.K + (size_t)(c.g0 + c.g) * Q4_GROUP) +
                           lane);
     if (NORM) {
+        // a predicated load, not a branch: tasks without a norm take g = 1
         norm = c.gn != nullptr;
-        if (norm) gv = __ldg(reinterpret_cast<const float2 *>(c.gn + (size_t)(c.g0 + c.g) * Q4_GROUP) + lane);
+        const float2 *gp = reinterpret_cast<const float2 *>((norm ? c.gn : c.x) + (size_t)(c.g0 + c.g) * Q4_GROUP) + lane;
+        const float2 g = __ldg(gp);
+        gv = norm ? g : make_float2(1.0f, 1.0f);
     }
 }
 
@@ -400,7 +414,6 @@ __device__ __forceinline__ void run_item_i8(const Launch &L, const Task &T, int 
     float iss[BB];
 #pragma unroll
     for (int b = 0; b < BB; ++b) iss[b] = 0.0f;
-    const bool norm = NORM && T.gn != nullptr;
 
     for (int st = 0; st < nsteps; ++st) {
         const int tt = DUAL ? (st & 1) : 0;
@@ -415,7 +428,7 @@ __device__ __forceinline__ void run_item_i8(const Launch &L, const Task &T, int 
         I8X<BB> &cur = xs[P.par];
         if (tt == 0) {
             mma_step_i8<BB>(src, cur, acc[0], lane, sel);
-            if (norm) {
+            if (NORM) {
 #pragma unroll
                 for (int b = 0; b < BB; ++b) iss[b] += cur.ss[b];  // groups in ascending order
             }

@@ -53,6 +53,7 @@ struct __align__(16) MbSmem {
     uint2 b[2][4][MbShape<BP>::NT][2][32];  // [buffer][group][n-tile][k-step][lane]: b0, b1
     float up[2][4][BP];                     // 2^e per (group, batch column)
     float ss[2][4][BP];                     // fused RMSNorm: sum of h^2 per (group, batch column)
+    float nr[BP];                           // fused RMSNorm: scale per batch column (split reduction)
     unsigned last;                          // split ticket of this CTA's item
 };
 
@@ -217,30 +218,36 @@ __device__ __forceinline__ void mb_prep(MbSmem<BP> &sm, int par, const MbCursor 
 #pragma unroll
         for (int j = 0; j < 4; ++j)
             v[j] = live ? __ldg(reinterpret_cast<const float2 *>(xp + 8 * j)) : make_float2(0.0f, 0.0f);
-        if (NORM && c.T->gn != nullptr) {
+        float ssq = 0.0f;
+        if (NORM) {
             // fused RMSNorm: v is the raw input h; the group is prepared as h * g
-            const float *gp = c.T->gn + (xp - (c.T->x + (size_t)(live ? b : 0) * c.T->K));
+            // (g = 1 for the launch's tasks without a norm: predicated, no branch)
+            const float *gn = c.T->gn;
+            const bool nrm = gn != nullptr;
+            const float *gp = (nrm ? gn : c.T->x) + (xp - (c.T->x + (size_t)(live ? b : 0) * c.T->K));
             float q = 0.0f;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 q = fmaf(v[j].x, v[j].x, q);
                 q = fmaf(v[j].y, v[j].y, q);
-                const float2 g = live ? __ldg(reinterpret_cast<const float2 *>(gp + 8 * j)) : make_float2(0.0f, 0.0f);
+                const float2 gl = __ldg(reinterpret_cast<const float2 *>(gp + 8 * j));
+                const float2 g = nrm ? gl : make_float2(1.0f, 1.0f);
                 v[j].x *= g.x;
                 v[j].y *= g.y;
             }
-            q += __shfl_xor_sync(0xffffffffu, q, 1);
-            q += __shfl_xor_sync(0xffffffffu, q, 2);
-            q += __shfl_xor_sync(0xffffffffu, q, 4);
-            if (gi < c.ncg && (r & 7) == 0) sm.ss[par][gi][b] = q;
+            ssq = q;
         }
         float m = 0.0f;
 #pragma unroll
         for (int j = 0; j < 4; ++j) m = fmaxf(m, fmaxf(fabsf(v[j].x), fabsf(v[j].y)));
-        // the 8 threads of (gi, b) are lanes 8k .. 8k + 7 of one warp
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        // the 8 threads of (gi, b) are lanes 8k .. 8k + 7 of one warp; with NORM
+        // the sum of h^2 shares the shuffle rounds
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if (NORM) ssq += __shfl_xor_sync(0xffffffffu, ssq, o);
+        }
+        if (NORM && gi < c.ncg && (r & 7) == 0) sm.ss[par][gi][b] = ssq;
         const uint32_t e = max((__float_as_uint(m) >> 23) & 0xffu, 22u);  // as prep_group_i8
         const bool nz = m > 0.0f;
         const float f = nz ? __uint_as_float((275u - e) << 23) : 1.0f;
@@ -395,6 +402,10 @@ __device__ __forceinline__ void mb_finish(const Task &T, int rb, int s, int B, f
     __syncthreads();
     if (sm.last == 0) return;
     __threadfence();
+    if (NORM && norm) {  // every column's scale once, then shared
+        if (tid < B) sm.nr[tid] = norm_scale(T, split_sumsq(T, rb, tid, B));
+        __syncthreads();
+    }
     const int row = rb * Q4_BLOCK_ROWS + tid;  // 128 threads, 128 rows
     if (row < T.N) {
         const size_t split_stride = (size_t)planes * B * T.N;
@@ -406,9 +417,8 @@ __device__ __forceinline__ void mb_finish(const Task &T, int rb, int s, int B, f
                 if (dual) s1 += __ldcg(p0 + sp * split_stride + (size_t)B * T.N);
             }
             if (NORM && norm) {
-                const float nr = norm_scale(T, split_sumsq(T, rb, b, B));
-                s0 *= nr;
-                s1 *= nr;
+                s0 *= sm.nr[b];
+                s1 *= sm.nr[b];
             }
             const size_t idx = (size_t)b * T.N + row;
             put_y(T, idx, finish(s0, s1, T.op, T.add, idx));
@@ -470,7 +480,7 @@ __global__ void __launch_bounds__(kMbThreads, BP <= 8 ? 4 : 3) q4_gemv_mb_kernel
                     mb_tile<BP>(tr[sl], sm, par, gi, lane, acc[HAS_DUAL ? 1 : 0]);
                 } else {
                     mb_tile<BP>(tr[sl], sm, par, gi, lane, acc[0]);
-                    if (NORM && cur.T->gn != nullptr) {  // fused RMSNorm: groups in ascending order
+                    if (NORM) {  // fused RMSNorm: groups in ascending order
 #pragma unroll
                         for (int bb = 0; bb < S::NBB; ++bb) {
                             iss[bb][0] += sm.ss[par][gi][8 * bb + 2 * c];
