@@ -179,8 +179,7 @@ void q4rdna_plan_destroy(q4rdna_plan *plan);
  * x_host mirrors it byte for byte; [y_dev, y_dev + y_bytes) must hold every
  * output and y_host receives it byte for byte (pinned host memory lets the
  * copies run asynchronously).  The plan is cut into `segments` runs of
- * consecutive descriptors with about equal weight bytes (0: one per 192 MiB of
- * weights, at most 16).  Segment s's
+ * consecutive descriptors with about equal weight bytes (0: 3).  Segment s's
  * activations are copied in on a library copy stream, its GEMVs wait for that
  * copy only, and its outputs are copied out on a second copy stream as soon
  * as they are written.  Consecutive segments run on two library streams, so a
@@ -197,12 +196,11 @@ q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *
 
 /* How q4rdna_plan_run executes the plan: as `segments` launches of consecutive
  * descriptors (about equal weight bytes) that alternate between two library
- * streams and are joined to `stream` at the end (0, the default: one segment
- * per 192 MiB of weights, at most 16; 1 = one launch).  Consecutive launches overlap: one segment's last items
- * share the SMs with the next segment's first ones, and each launch streams a
- * compact range of the weights.  Measured on the Qwen3-8B step: 935 us as one
- * launch, 786 us as 16.  Results are identical.  With a gather
- * (q4rdna_plan_set_gather) the flag exchange follows the last segment. */
+ * streams and are joined to `stream` at the end.  1 (the default; also 0) =
+ * one launch, which is the fastest with the plan's own split-K choice; more
+ * segments pay off only for plans whose descriptors force small items.
+ * Results are identical.  With a gather (q4rdna_plan_set_gather) the flag
+ * exchange follows the last segment. */
 q4rdna_status q4rdna_plan_set_segments(q4rdna_plan *plan, int segments);
 
 /* ---- tensor parallelism: the all-gather fused into the plan kernel ----

@@ -38,6 +38,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <atomic>
 #include <cstdint>
 #include <cstdio>
@@ -691,6 +692,14 @@ size_t plan_ws_bytes_for(int N, int B, int S, int op, bool norm) {
            (norm ? align256(sumsq_bytes(N, B, S)) : 0);
 }
 
+// Work items per resident warp (or tile-path CTA) that a plan's split-K choice
+// aims at; Q4RDNA_PLAN_ITEMS overrides the default for A/B measurements.
+double plan_items_per_worker() {
+    const char *e = std::getenv("Q4RDNA_PLAN_ITEMS");
+    const double v = (e != nullptr && *e != '\0') ? std::atof(e) : 0.0;
+    return v > 0.0 ? std::min(v, 1024.0) : 2.0;
+}
+
 // The fused RMSNorm runs in the int8 batch-1 kernel and the tile path, not in
 // the A/B variants (Q4RDNA_KERNEL=ldg|i8tma).
 bool norm_supported(int B) { return B >= tile_min_batch() || variant() == kI8; }
@@ -806,16 +815,14 @@ __global__ void q4_gather_signal_kernel(const __grid_constant__ GatherSignal a) 
     if (i == kGatherTries) atomicOr(&g_fault, kFaultGatherTimeout);
 }
 
-// Default segment count of a plan run: one segment per kSegmentBytes of
-// weights, at most kMaxSegments.  Measured: the Qwen3-8B step (3.69 GB) is
-// fastest as 16 segments (230 MB each); an eighth of it per GPU (461 MB) is
-// 2x slower as 16 segments than as one launch, because every launch has a
-// fixed cost of ~10-15 us that the overlap does not hide.
-constexpr uint64_t kSegmentBytes = 192ull << 20;
-constexpr int kMaxSegments = 16;
-int default_segments(uint64_t weight_bytes) {
-    return (int)std::max<uint64_t>(1, std::min<uint64_t>(kMaxSegments, weight_bytes / kSegmentBytes));
-}
+// Segment counts.  Plan runs default to one launch: with the plan-wide split
+// choice the items are large and few per warp, and segment launches that
+// overlap (two streams) leave SMs idle between segments (Qwen3-8B step: 631 us
+// as one launch, 705 us as 2, 750 us as 4).  q4rdna_plan_run_host defaults to 3
+// segments, the measured best trade between hidden copies and that cost
+// (e2e 820 us; 856 us with 1 segment, 865 us with 4).
+constexpr int kHostSegments = 3;
+
 
 struct q4rdna_plan {
     int device = -1;
@@ -840,7 +847,7 @@ struct q4rdna_plan {
     };
     std::vector<Segment> segs;
     int seg_request = -1;
-    int run_segments = 0;  // q4rdna_plan_run: 0 = default_segments(weight_bytes), 1 = one launch
+    int run_segments = 1;  // q4rdna_plan_run: segment launches (1 = one launch, the default)
     const void *seg_x = nullptr, *seg_y = nullptr;
     cudaStream_t h2d = nullptr, d2h = nullptr;
     cudaStream_t comp[2] = {nullptr, nullptr};  // segments alternate, so one's tail overlaps the next
@@ -955,6 +962,21 @@ q4rdna_status q4rdna_plan_create(const q4rdna_gemv_desc *descs, int count, int B
     size_t ws_total = 0;
     long long items = 0;
     uint64_t wbytes = 0, abytes = 0;
+    // Split-K only as far as the whole plan needs it: every split adds partial
+    // stores, a fence and a reduction per item, which on the Qwen3-8B step cost
+    // more than the imbalance of unsplit items (624 us per step unsplit, 949 us
+    // with ~64 KB items).  Each task gets the split that gives the plan about
+    // plan_items_per_worker() items per resident warp (CTA on the tile path).
+    long long total_rb = 0;
+    bool any_dual_task = false;
+    for (int i = 0; i < count; ++i) {
+        if (descs[i].N > 0) total_rb += (descs[i].N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
+        any_dual_task = any_dual_task || descs[i].op == Q4RDNA_OP_SWIGLU;
+    }
+    const long long workers = (long long)d.sms * d.occ[variant()][batch_class(B)][any_dual_task] *
+                              kernel_cfg(variant(), B, any_dual_task).warps;
+    const double want_items = plan_items_per_worker() * (double)workers;
+    const int plan_split = total_rb > 0 ? (int)std::max(1.0, std::ceil(want_items / (double)total_rb)) : 1;
     for (int i = 0; i < count; ++i) {
         const q4rdna_gemv_desc &e = descs[i];
         q4rdna_status st = check_shape(e.N, e.K, B);
@@ -970,15 +992,7 @@ q4rdna_status q4rdna_plan_create(const q4rdna_gemv_desc *descs, int count, int B
         const int planes = e.op == Q4RDNA_OP_SWIGLU ? 2 : 1;
         const int G = e.K / Q4_GROUP;
         const int RB = (e.N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
-        // Plans hold many tensors, so items are sized by bytes (~64 KB of tiles for
-        // the warp-item kernels, ~256 KB for the CTA-item tile path) instead of by
-        // occupancy: split overhead stays ~1% of the stream.
-        int req = e.split;
-        if (req <= 0) {
-            const int item_bytes = B >= tile_min_batch() ? 4 * 65536 : 65536;
-            const int gs = std::max(1, item_bytes / (Q4_BLOCK_TILES * Q4_TILE_BYTES * planes));
-            req = (G + gs - 1) / gs;
-        }
+        const int req = e.split > 0 ? e.split : std::min(plan_split, G);
         const Split sp = make_split(G, req);
         Task &T = host[i];
         T.w = e.tiles; T.w2 = e.gate_tiles; T.x = e.x; T.add = e.add; T.y = e.y;
@@ -1030,7 +1044,7 @@ q4rdna_status q4rdna_plan_run(q4rdna_plan *plan, q4rdna_stream_t stream) {
     if (plan == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev != plan->device) return Q4RDNA_ERR_DEVICE;
-    const int nseg = plan->run_segments > 0 ? plan->run_segments : default_segments(plan->weight_bytes);
+    const int nseg = std::max(1, plan->run_segments);
     const bool segmented = nseg > 1 && plan->count > 1;
     if (segmented) {
         const int want = std::min(nseg, plan->count);
@@ -1287,7 +1301,7 @@ q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *
     if (plan->gather) return Q4RDNA_ERR_UNSUPPORTED;
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev != plan->device) return Q4RDNA_ERR_DEVICE;
-    const int want = segments == 0 ? default_segments(plan->weight_bytes) : segments;
+    const int want = segments == 0 ? kHostSegments : segments;
     if (plan->seg_request != std::max(1, std::min(want, plan->count)) || plan->seg_x != x_dev ||
         plan->seg_y != y_dev) {
         const q4rdna_status st = build_segments(plan, want, static_cast<const uint8_t *>(x_dev), x_bytes,
@@ -1304,7 +1318,7 @@ q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *
 
 q4rdna_status q4rdna_plan_set_segments(q4rdna_plan *plan, int segments) {
     if (plan == nullptr || segments < 0) return Q4RDNA_ERR_INVALID_ARGUMENT;
-    plan->run_segments = segments;
+    plan->run_segments = segments == 0 ? 1 : segments;
     return Q4RDNA_OK;
 }
 

@@ -303,7 +303,7 @@ class Plan:
 
     def set_segments(self, segments: int):
         """run() as `segments` overlapping launches (q4rdna_plan_set_segments;
-        1 = one launch, 0 = the library default: one per 192 MiB of weights, at most 16)."""
+        1 or 0 = one launch, the default)."""
         check(_lib().q4rdna_plan_set_segments(self._h, segments), "plan_set_segments")
 
     def run_host(self, x_host, x_dev, y_dev, y_host, segments: int = 0, stream=None):
