@@ -824,6 +824,31 @@ __global__ void q4_gather_signal_kernel(const __grid_constant__ GatherSignal a) 
 constexpr int kHostSegments = 3;
 
 
+// Device copy of a task table in launch order: tasks with the longest items
+// first (stable), item_begin renumbered from 0.  The persistent kernels take
+// items round-robin, so the last round then consists of the shortest items
+// (longest-processing-time-first list scheduling); results do not depend on
+// the order.
+Task *upload_tasks(std::vector<Task> t) {
+    std::stable_sort(t.begin(), t.end(), [](const Task &a, const Task &b) {
+        const long long ca = (long long)a.Gs * (a.op == Q4RDNA_OP_SWIGLU ? 2 : 1);
+        const long long cb = (long long)b.Gs * (b.op == Q4RDNA_OP_SWIGLU ? 2 : 1);
+        return ca > cb;
+    });
+    long long items = 0;
+    for (Task &T : t) {
+        T.item_begin = items;
+        items += (long long)T.RB * T.S;
+    }
+    Task *d = nullptr;
+    if (cudaMalloc(&d, sizeof(Task) * t.size()) != cudaSuccess) return nullptr;
+    if (cudaMemcpy(d, t.data(), sizeof(Task) * t.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaFree(d);
+        return nullptr;
+    }
+    return d;
+}
+
 struct q4rdna_plan {
     int device = -1;
     int count = 0, B = 1, nb = 1, grid = 1;
@@ -1024,8 +1049,7 @@ q4rdna_status q4rdna_plan_create(const q4rdna_gemv_desc *descs, int count, int B
                                                   align256(partial_bytes(T.N, B, T.S, T.op)));
         }
     }
-    if (cudaMalloc(&p->table, sizeof(Task) * count) != cudaSuccess ||
-        cudaMemcpy(p->table, host.data(), sizeof(Task) * count, cudaMemcpyHostToDevice) != cudaSuccess) {
+    if ((p->table = upload_tasks(host)) == nullptr) {
         q4rdna_plan_destroy(p);
         return Q4RDNA_ERR_CUDA;
     }
@@ -1115,8 +1139,7 @@ q4rdna_status q4rdna_plan_set_gather(q4rdna_plan *plan, int world, int rank, con
             for (int p = 0; p < world; ++p) T.mirror[p] = g[p] + (size_t)rank * rank_floats + off;
         }
         plan->ghost[par] = t;
-        if (cudaMalloc(&plan->gtable[par], sizeof(Task) * t.size()) != cudaSuccess ||
-            cudaMemcpy(plan->gtable[par], t.data(), sizeof(Task) * t.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+        if ((plan->gtable[par] = upload_tasks(t)) == nullptr) {
             for (Task *&gt : plan->gtable) {
                 if (gt) cudaFree(gt);
                 gt = nullptr;
@@ -1175,7 +1198,6 @@ q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t
         std::vector<Task> t(p->host.begin() + first, p->host.begin() + last);
         const long long base = t.front().item_begin;
         for (Task &T : t) {
-            T.item_begin -= base;
             const uint8_t *x = reinterpret_cast<const uint8_t *>(T.x);
             const uint8_t *y = reinterpret_cast<const uint8_t *>(T.y);
             const size_t xn = (size_t)p->B * T.K * sizeof(float), yn = (size_t)p->B * T.N * sizeof(float);
@@ -1191,17 +1213,13 @@ q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t
         sg.grid = grid_for(sg.items, p->B, p->dual, d);
         p->segs.push_back(sg);  // owned by the plan from here on (freed on failure paths below)
         q4rdna_plan::Segment &g = p->segs.back();
-        if (cudaMalloc(&g.table, sizeof(Task) * t.size()) != cudaSuccess ||
-            cudaMemcpy(g.table, t.data(), sizeof(Task) * t.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+        if ((g.table = upload_tasks(t)) == nullptr ||
             cudaEventCreateWithFlags(&g.x_ready, cudaEventDisableTiming) != cudaSuccess ||
             cudaEventCreateWithFlags(&g.y_ready, cudaEventDisableTiming) != cudaSuccess)
             return Q4RDNA_ERR_CUDA;
         for (int par = 0; p->gather && par < 2; ++par) {
             std::vector<Task> gt(p->ghost[par].begin() + first, p->ghost[par].begin() + last);
-            for (Task &T : gt) T.item_begin -= base;
-            if (cudaMalloc(&g.gtable[par], sizeof(Task) * gt.size()) != cudaSuccess ||
-                cudaMemcpy(g.gtable[par], gt.data(), sizeof(Task) * gt.size(), cudaMemcpyHostToDevice) != cudaSuccess)
-                return Q4RDNA_ERR_CUDA;
+            if ((g.gtable[par] = upload_tasks(gt)) == nullptr) return Q4RDNA_ERR_CUDA;
         }
         first = last;
     }
