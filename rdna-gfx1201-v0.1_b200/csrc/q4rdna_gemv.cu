@@ -494,7 +494,7 @@ __global__ void q4_dequant_kernel(const uint8_t *tiles, float *W, int N, int K) 
 // ------------------------------------------------------------------ host side
 
 constexpr int kMaxDevices = 64;
-constexpr int kMaxPassBatch = 4;  // batch columns of the batch-1 kernels; above: the tile path
+constexpr int kMaxPassBatch = 4;  // batch columns the batch-1 kernels can take (BB <= 4)
 std::atomic<uint64_t> g_launches{0};
 
 // Kernel variants: the int8 tensor-core kernel with register loads (default,
@@ -525,7 +525,7 @@ constexpr int kBatchClasses = 5;
 int batch_class(int pb) { return pb <= 1 ? 0 : pb == 2 ? 1 : pb <= 4 ? 2 : pb <= 8 ? 3 : 4; }
 int class_batch(int bc) { return bc == 0 ? 1 : bc == 1 ? 2 : bc == 2 ? 4 : bc == 3 ? 8 : 16; }
 
-// Tile path for B = 5..16 (q4rdna_gemv_mb.cuh): one work item per CTA.
+// Tile path for B >= tile_min_batch() (q4rdna_gemv_mb.cuh): one work item per CTA.
 template <bool NORM>
 KernelCfg mb_cfg_n(int pb, bool dual) {
     if (pb <= 8)
@@ -758,7 +758,7 @@ q4rdna_status gemv_common(int op, const uint8_t *w, const uint8_t *w2, const flo
         ticket = static_cast<unsigned *>(ws);
         part = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + kTicketArea);
     }
-    // One launch for the whole batch: B <= 4 on the batch-1 kernels, B = 5..16
+    // One launch for the whole batch: B < tile_min_batch() on the batch-1 kernels, the rest
     // on the tile path; the weights are streamed once.
     Launch L{};
     L.table = nullptr;

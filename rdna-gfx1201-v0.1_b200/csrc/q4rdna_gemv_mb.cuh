@@ -1,10 +1,10 @@
-// Small-batch tile path, B = 5..16 activation columns (included into
+// Small-batch tile path, B = 3..16 activation columns (included into
 // q4rdna_gemv.cu inside namespace q4, after q4rdna_gemv_i8.cuh).
 //
-// At B >= 5 the work is a dense contraction: every weight meets B activations.
+// At B >= 3 the work is a dense contraction: every weight meets B activations.
 // The batch-1 kernel's fragment mapping spends most of each MMA on zeros (it
 // keeps rows in the K slots so that lanes need no transposition), which is
-// right for B <= 4 and wasteful above it.  This kernel uses the full
+// right for B <= 2 and wasteful above it.  This kernel uses the full
 // m16n8k32 fragment instead:
 //
 //   * one CTA (4 warps) owns one work item: 128 rows (4 row tiles) x a split of

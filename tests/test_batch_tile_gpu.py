@@ -1,4 +1,4 @@
-"""The small-batch tile path (B = 5..16, q4_gemv_mb_kernel) against the CPU
+"""The small-batch tile path (B = 3..16, q4_gemv_mb_kernel) against the CPU
 oracle: single calls over the split range, the add / SwiGLU epilogues, plans,
 ragged row counts and extreme activation columns.  Needs a B200."""
 import os
