@@ -490,6 +490,7 @@ __global__ void q4_dequant_kernel(const uint8_t *tiles, float *W, int N, int K) 
 #include "q4rdna_gemv_i8.cuh"
 #include "q4rdna_gemv_i8_tma.cuh"
 #include "q4rdna_gemv_mb.cuh"
+#include "q4rdna_gemv_mbh.cuh"
 
 // ------------------------------------------------------------------ host side
 
@@ -525,14 +526,33 @@ constexpr int kBatchClasses = 5;
 int batch_class(int pb) { return pb <= 1 ? 0 : pb == 2 ? 1 : pb <= 4 ? 2 : pb <= 8 ? 3 : 4; }
 int class_batch(int bc) { return bc == 0 ? 1 : bc == 1 ? 2 : bc == 2 ? 4 : bc == 3 ? 8 : 16; }
 
-// Tile path for B >= tile_min_batch() (q4rdna_gemv_mb.cuh): one work item per CTA.
+// Tile path for B >= tile_min_batch(): one work item per CTA.  The int8
+// kernel (q4rdna_gemv_mb.cuh) by default; Q4RDNA_TILE=f16 selects the f16 one
+// (q4rdna_gemv_mbh.cuh), kept for A/B measurements: on the Qwen3-8B step it
+// took 1695 / 1729 / 3441 us at B = 4 / 8 / 16 against 1249 / 1281 / 2373 us
+// for the int8 kernel (long-scoreboard bound at 142 registers, 3 CTAs/SM).
+bool tile_i8() {
+    static const bool v = [] {
+        const char *e = std::getenv("Q4RDNA_TILE");
+        return e == nullptr || std::strcmp(e, "f16") != 0;
+    }();
+    return v;
+}
+
 template <bool NORM>
 KernelCfg mb_cfg_n(int pb, bool dual) {
+    if (tile_i8()) {
+        if (pb <= 8)
+            return dual ? KernelCfg{(const void *)q4_gemv_mb_kernel<8, true, NORM>, kMbThreads, 0, 1}
+                        : KernelCfg{(const void *)q4_gemv_mb_kernel<8, false, NORM>, kMbThreads, 0, 1};
+        return dual ? KernelCfg{(const void *)q4_gemv_mb_kernel<16, true, NORM>, kMbThreads, 0, 1}
+                    : KernelCfg{(const void *)q4_gemv_mb_kernel<16, false, NORM>, kMbThreads, 0, 1};
+    }
     if (pb <= 8)
-        return dual ? KernelCfg{(const void *)q4_gemv_mb_kernel<8, true, NORM>, kMbThreads, 0, 1}
-                    : KernelCfg{(const void *)q4_gemv_mb_kernel<8, false, NORM>, kMbThreads, 0, 1};
-    return dual ? KernelCfg{(const void *)q4_gemv_mb_kernel<16, true, NORM>, kMbThreads, 0, 1}
-                : KernelCfg{(const void *)q4_gemv_mb_kernel<16, false, NORM>, kMbThreads, 0, 1};
+        return dual ? KernelCfg{(const void *)q4_gemv_mbh_kernel<8, true, NORM>, kMbThreads, 0, 1}
+                    : KernelCfg{(const void *)q4_gemv_mbh_kernel<8, false, NORM>, kMbThreads, 0, 1};
+    return dual ? KernelCfg{(const void *)q4_gemv_mbh_kernel<16, true, NORM>, kMbThreads, 0, 1}
+                : KernelCfg{(const void *)q4_gemv_mbh_kernel<16, false, NORM>, kMbThreads, 0, 1};
 }
 KernelCfg mb_cfg(int pb, bool dual, bool norm) { return norm ? mb_cfg_n<true>(pb, dual) : mb_cfg_n<false>(pb, dual); }
 

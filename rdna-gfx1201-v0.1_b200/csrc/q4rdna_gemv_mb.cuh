@@ -339,10 +339,11 @@ __device__ __forceinline__ void mb_tile(const MbTileRegs &r, const MbSmem<BP> &s
 // CTA that arrives last at row block rb, add the splits in ascending order.
 // iss: fused RMSNorm (NORM kernels), the item's sum of h^2 per (batch block,
 // column) of this lane.
-template <int BP, bool HAS_DUAL, bool NORM>
+// Sm: the kernel's shared block (members `last` and `nr[BP]`).
+template <int BP, bool HAS_DUAL, bool NORM, class Sm>
 __device__ __forceinline__ void mb_finish(const Task &T, int rb, int s, int B, float (&acc)[HAS_DUAL ? 2 : 1][4][BP / 8][2],
                                           const float (&iss)[BP / 8][2], bool dual, bool valid, int tile_row,
-                                          int lane, int tid, MbSmem<BP> &sm) {
+                                          int lane, int tid, Sm &sm) {
     using S = MbShape<BP>;
     const int g = lane >> 2, c = lane & 3;
     const int row0 = tile_row * Q4_TILE_ROWS + 4 * g;

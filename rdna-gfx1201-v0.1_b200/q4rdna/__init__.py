@@ -416,9 +416,10 @@ _KERNELS = {"i8": "q4::q4_gemv_i8_kernel", "i8tma": "q4::q4_gemv_i8_tma_kernel",
 
 
 def kernel_name(B: int = 1) -> str:
-    """Name of the GEMV kernel the library launches for batch B: the tile path
-    for B = 3..16, else the int8 tensor-core kernel unless Q4RDNA_KERNEL selects
-    another variant (read by the library at its first launch, same names)."""
+    """Name of the GEMV kernel the library launches for batch B: the int8 tile
+    path for B = 3..16 (the f16 tile path when Q4RDNA_TILE=f16), else the int8
+    tensor-core kernel unless Q4RDNA_KERNEL selects another variant (read by the
+    library at its first launch, same names)."""
     if B >= int(os.environ.get("Q4RDNA_TILE_MIN_BATCH") or 3):
-        return "q4::q4_gemv_mb_kernel"
+        return "q4::q4_gemv_mbh_kernel" if os.environ.get("Q4RDNA_TILE") == "f16" else "q4::q4_gemv_mb_kernel"
     return _KERNELS.get(os.environ.get("Q4RDNA_KERNEL") or "i8", _KERNELS["i8"])

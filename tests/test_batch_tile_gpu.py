@@ -1,6 +1,8 @@
-"""The small-batch tile path (B = 3..16, q4_gemv_mb_kernel) against the CPU
-oracle: single calls over the split range, the add / SwiGLU epilogues, plans,
-ragged row counts and extreme activation columns.  Needs a B200."""
+"""The small-batch tile path (B = 3..16) against the CPU oracle: the int8
+q4_gemv_mb_kernel, or the f16 q4_gemv_mbh_kernel when the suite runs with
+Q4RDNA_TILE=f16 (the library reads it once, at its first launch).  Single calls
+over the split range, the add / SwiGLU epilogues, plans, ragged row counts and
+extreme activation columns.  Needs a B200."""
 import os
 
 import numpy as np
