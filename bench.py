@@ -254,12 +254,17 @@ def run_pack(args):
             "cpu_baseline": cpu, "gpu_launches": q4rdna.launch_count() - l0, "clocks": clk.summary()}
 
 
+QKV = (".attn_q.", ".attn_k.", ".attn_v.")
+
+
 def build_step(model: str, rank: int, world: int, device, seed: int, layers: int = 0, B: int = 1,
-               norm: bool = False):
+               norm: bool = False, hybrid: bool = False):
     """Weights (this rank's row shard of every tensor), activations and outputs
     of one decode step, laid out by q4rdna.tp.Layout so that a step's inputs and
     outputs are each one contiguous buffer (one copy each way for the
-    end-to-end leg, one all-gather for tensor parallelism)."""
+    end-to-end leg, one all-gather for tensor parallelism).  hybrid: the
+    reference's qkv-fallback scope (source/q4rdna.cu:685-691), attn_q/k/v in
+    Q4_K (block_q4_K rows), every other tensor in Q4_RDNA."""
     import torch
 
     from q4rdna import synth, tp
@@ -277,21 +282,32 @@ def build_step(model: str, rank: int, world: int, device, seed: int, layers: int
     g = torch.Generator(device=device)
     g.manual_seed(seed)  # same activations on every rank (replicated x)
     x_all.normal_(generator=g)
+    import q4rdna
+
     descs, xo = [], 0
-    wbytes = abytes = 0
+    wbytes = abytes = nweights = 0
     for i, s in enumerate(lay.slots):
         # each rank draws its own shard (same distributions; the shard of one
         # full tensor is a byte slice, q4rdna.tp.shard_tiles)
-        t = synth.tiles_torch(s.rows, s.K, seed + 1 + i * world + rank, device)
+        q4k = hybrid and any(q in names[i][0] for q in QKV)
+        if q4k:
+            t = synth.q4k_torch(s.rows, s.K, seed + 1 + i * world + rank, device)
+            tb = synth.q4k_bytes(s.rows, s.K)
+        else:
+            t = synth.tiles_torch(s.rows, s.K, seed + 1 + i * world + rank, device)
+            tb = s.rows * s.K * 34 // 64
         d = {"tiles": t, "x": x_all[B * xo:B * (xo + s.K)].view(B, s.K), "y": lay.local_view(y_all, i)}
+        if q4k:
+            d["format"] = q4rdna.FORMAT_Q4K
         if norm:  # x is the raw hidden state; the plan normalises it on the fly
             d["norm_weight"] = torch.ones(s.K, dtype=torch.float32, device=device)
             d["norm_eps"] = 1e-6
         descs.append(d)
         xo += s.K
-        wbytes += s.rows * s.K * 34 // 64
-        abytes += s.rows * s.K * 34 // 64 + 4 * B * (s.K + s.rows)
-    return descs, x_all, y_all, wbytes, abytes, len(names), lay
+        wbytes += tb
+        nweights += s.rows * s.K
+        abytes += tb + 4 * B * (s.K + s.rows)
+    return descs, x_all, y_all, wbytes, abytes, len(names), lay, nweights
 
 
 def run_ours(args):
@@ -316,13 +332,15 @@ def run_ours(args):
         raise SystemExit("libq4rdna.so not built")
 
     B = args.batch
-    descs, x_all, y_all, wbytes, abytes, ntensors, lay = build_step(args.model, rank, world, dev, args.seed,
-                                                                   args.layers, B, args.norm)
+    if args.hybrid and args.norm:
+        raise SystemExit("--hybrid takes no --norm (the Q4_K kernel has no fused RMSNorm)")
+    descs, x_all, y_all, wbytes, abytes, ntensors, lay, nweights = build_step(
+        args.model, rank, world, dev, args.seed, args.layers, B, args.norm, args.hybrid)
     plan = q4rdna.Plan(descs, B=B)
     plan.set_segments(args.run_segments)
     info = plan.info()
     stream = torch.cuda.current_stream()
-    p2p = world > 1 and args.gather == "p2p"
+    p2p = world > 1 and args.gather == "p2p" and not args.hybrid  # the fused gather has no Q4_K epilogue
     gathered = torch.empty(y_all.numel() * world, device=dev) if world > 1 and not p2p else None
     pg = tp.PeerGather(plan, lay, y_all) if p2p else None
 
@@ -362,6 +380,28 @@ def run_ours(args):
     launches = q4rdna.launch_count() - l0
     ms_total = t0.elapsed_time(t1)
     kern_ms = statistics.mean(a.elapsed_time(b) for a, b in k_ev)
+    q4k_leg = None
+    if args.hybrid:
+        # the Q4_K tensors alone, as one plan: the Q4_K kernel's own roofline
+        kd = [d for d in descs if d.get("format") == q4rdna.FORMAT_Q4K]
+        kplan = q4rdna.Plan(kd, B=B)
+        kbytes = sum(d["tiles"].numel() + 4 * B * (d["x"].shape[-1] + d["y"].shape[-1]) for d in kd)
+        for _ in range(max(3, args.warmup)):
+            kplan.run(stream)
+        barrier()
+        kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for i in range(args.steps):
+            kev[i][0].record(stream)
+            kplan.run(stream)
+            kev[i][1].record(stream)
+        barrier()
+        k_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+        kplan.close()
+        kpk, _ = hbm_peak()
+        q4k_leg = {"kernel": "q4k::q4k_gemv_kernel (plan of the Q4_K tensors alone)", "tensors": len(kd),
+                   "algo_bytes": kbytes, "kernel_us": round(k_ms * 1e3, 2),
+                   "achieved": round(kbytes / (k_ms * 1e-3) / 1e9, 1), "frac": round(kbytes / (k_ms * 1e-3) / 1e9 / kpk, 4),
+                   "traffic": ncu_traffic(f"q4k_{args.model}_b{B}")}
 
     # end-to-end: pinned host activations in, outputs out, every step
     x_host = torch.empty(x_all.numel(), dtype=torch.float32, pin_memory=True)
@@ -400,7 +440,7 @@ def run_ours(args):
     out = None
     if rank == 0:
         cpu = None
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and not args.hybrid:
             v, kind, thr, sample = reference_cpu_rate(args.cpu_seconds, cpu_count())
             cpu = {"value": round(v, 3), "unit": UNIT, "cores": thr, "kind": kind, "sample": sample}
         out = {
@@ -408,12 +448,15 @@ def run_ours(args):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
             "us_per_step": round(step_ms * 1e3, 2), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int4 x f32 (fp16 scales, f32 accumulate)",
-            "data": "synthetic: uniform int4 codes, fp16 scales |N(0,1)|*0.003, x ~ N(0,1) f32 (no Qwen3 weights offline)",
+            "data": "synthetic: uniform int4 codes, fp16 scales |N(0,1)|*0.003, x ~ N(0,1) f32 (no Qwen3 weights offline)"
+                    + ("; Q4_K tensors: uniform quant and 6-bit scale bytes, d and dmin fp16((0.5+|N(0,1)|)*2e-4)"
+                       if args.hybrid else ""),
             "config": {"workload": f"{args.model} decode-step weight stream: {ntensors} GEMVs batch {B}"
                                    + (f" (first {args.layers} layers only)" if args.layers else "")
+                                   + (", qkv-fallback hybrid: attn_q/k/v in Q4_K, the rest in Q4_RDNA" if args.hybrid else "")
                                    + (f", rows sharded over {world} GPUs + " + ("all-gather fused into the plan kernel (P2P stores)"
                                       if p2p else "NCCL all-gather") if world > 1 else ""),
-                       "tensors": ntensors, "batch": B, "fused_rmsnorm": bool(args.norm), "flops_per_step": 2 * B * wbytes * world * 64 // 34,
+                       "tensors": ntensors, "batch": B, "fused_rmsnorm": bool(args.norm), "flops_per_step": 2 * B * nweights * world,
                        "weight_bytes_per_step": wbytes * world,
                        "algo_bytes_per_step": total_algo, "parallelism": f"tp{world}" if world > 1 else "none",
                        "l2": f"no flush: {wbytes * world / 1e9:.2f} GB streamed per step >> 126 MB L2",
@@ -421,12 +464,14 @@ def run_ours(args):
             "e2e": {"value": round(total_algo / (e2e_ms / args.steps * 1e-3) / 1e9, 2), "unit": UNIT,
                     "us_per_step": round(e2e_ms / args.steps * 1e3, 2),
                     "h2d_bytes_per_step": x_all.numel() * 4, "d2h_bytes_per_step": y_host.numel() * 4},
-            "roofline": {"bound": "hbm", "kernel": q4rdna.kernel_name(B) + (" (plan + fused gather)" if p2p else " (plan)"), "achieved": round(achieved, 1),
+            "roofline": {"bound": "hbm", "kernel": q4rdna.kernel_name(B) + (" + q4k::q4k_gemv_kernel" if args.hybrid else "")
+                         + (" (plan + fused gather)" if p2p else " (plan)"), "achieved": round(achieved, 1),
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "algo_bytes_per_launch": abytes, "kernel_us": round(kern_ms * 1e3, 2),
                          "traffic": ncu_traffic(f"{args.model}_tp{world}" + (f"_b{B}" if B > 1 else ""))},
             "cpu_baseline": cpu,
             "gpu_launches": launches,
+            **({"q4k": q4k_leg} if q4k_leg else {}),
             "clocks": clk.summary(),
         }
     if pg is not None:
@@ -484,6 +529,8 @@ def main():
                     help="e2e leg at N = 1: plan segments whose host copies overlap the GEMVs (0: library default)")
     ap.add_argument("--batch", type=int, default=1,
                     help="activation columns per GEMV (1..16; 3..16 run the tile path)")
+    ap.add_argument("--hybrid", action="store_true",
+                    help="the reference's qkv-fallback scope: attn_q/k/v as Q4_K tensors, the rest Q4_RDNA")
     ap.add_argument("--layers", type=int, default=0,
                     help="only the first L layers (small cases for profiling); 0 = the whole model")
     args = ap.parse_args()

@@ -137,6 +137,32 @@ q4rdna_status q4rdna_gemv_noalloc(const uint8_t *tiles, const float *x, float *y
  * (source/q4rdna.cu:346-371). */
 q4rdna_status q4rdna_dequant_f32(const uint8_t *tiles, float *W, int N, int K, q4rdna_stream_t stream);
 
+/* ---- Q4_K rows: the tensors the reference leaves on llama.cpp's stock path ----
+ * The qkv-fallback scope (source/q4rdna.cu:685-691, LLAMA_Q4_RDNA_SCOPE)
+ * routes attn_q/k/v to the caller's Q4_K kernel; the reference bench times a
+ * Q4_K GEMV (q4_k_gemv, source/q4rdna_gemv_bench.hip:93-135) beside its own.
+ * These entry points run such tensors on the GPU with the same stream and
+ * status conventions.  Layout (source/q4rdna_cpu_experiment.cpp:17, 102-135):
+ * a row is K/256 blocks of 144 bytes (fp16 d, fp16 dmin, 12 bytes of 6-bit
+ * scales and mins, 128 bytes of unsigned nibbles); weight = d * scale * q -
+ * dmin * min per 32-column sub-block.  K % 256 == 0; blocks 16-byte aligned,
+ * x 16-byte aligned, y and add 4-byte aligned; x must be finite. */
+#define Q4RDNA_Q4K_BLOCK 256
+#define Q4RDNA_Q4K_BLOCK_BYTES 144
+
+/* Bytes of an N x K Q4_K tensor (0 for a bad shape). */
+size_t q4rdna_q4k_bytes(int N, int K);
+
+/* y = W x (+ add when add != NULL), x f32 [B][K], y and add f32 [B][N],
+ * B in [1, Q4RDNA_MAX_BATCH].  No workspace and no allocation. */
+q4rdna_status q4rdna_q4k_gemv(const uint8_t *blocks, const float *x, const float *add, float *y, int N, int K,
+                              int B, q4rdna_stream_t stream);
+
+/* Debug: dense row-major W[N][K], bit-exact with the reference's
+ * dequantize_q4_k (source/q4rdna_cpu_experiment.cpp:112-135) on IEEE fp16
+ * decoding of d and dmin. */
+q4rdna_status q4rdna_q4k_dequant_f32(const uint8_t *blocks, float *W, int N, int K, q4rdna_stream_t stream);
+
 /* ---- multi-GEMV plans: many independent GEMVs in one persistent launch ----
  * One descriptor per GEMV; all share the batch B.  gate_tiles is used only by
  * Q4RDNA_OP_SWIGLU, add only by Q4RDNA_OP_ADD.  The plan copies the
@@ -156,7 +182,15 @@ typedef struct q4rdna_gemv_desc {
     /* fused RMSNorm (q4rdna_gemv_rmsnorm): norm weight [K] or NULL; x is then the raw input h */
     const float *norm_weight;
     float norm_eps;
+    /* weight format of `tiles`: Q4RDNA_FORMAT_Q4RDNA (0, the default) or
+     * Q4RDNA_FORMAT_Q4K (ggml block_q4_K rows; op PLAIN or ADD, no norm) */
+    int format;
 } q4rdna_gemv_desc;
+
+typedef enum q4rdna_format {
+    Q4RDNA_FORMAT_Q4RDNA = 0, /* 32 x 64 tiles of 1088 bytes (q4rdna.cu:20-24) */
+    Q4RDNA_FORMAT_Q4K = 1     /* ggml block_q4_K: 144 bytes per 256 weights of a row */
+} q4rdna_format;
 
 typedef struct q4rdna_plan q4rdna_plan;
 typedef struct q4rdna_plan_info {

@@ -56,6 +56,9 @@ if lib is not None:
     lib.q4o_select_scale.argtypes = [_f32p]
     lib.q4o_select_scale.restype = ctypes.c_uint16
     lib.q4o_pack_bf16.argtypes = [_u16p, _i64, _i64, _u8p, ctypes.c_int]
+    lib.q4o_q4k_dequant.argtypes = [_u8p, _i64, _i64, _f32p, _ci]
+    lib.q4o_q4k_gemv_f32.argtypes = [_u8p, _f32p, _f32p, _i64, _i64, _i64, _ci, _ci]
+    lib.q4o_q4k_gemv_f64.argtypes = [_u8p, _f32p, _f64p, _f64p, _i64, _i64, _i64, _ci, _ci]
     lib.q4o_silu.argtypes = [ctypes.c_float]
     lib.q4o_silu.restype = ctypes.c_float
 
@@ -81,6 +84,7 @@ if ref is not None:
     ref.q4ref_exp_float_to_fp16.restype = ctypes.c_uint16
     ref.q4ref_exp_fp16_to_float.argtypes = [ctypes.c_uint16]
     ref.q4ref_exp_fp16_to_float.restype = ctypes.c_float
+    ref.q4ref_exp_dequant_q4k.argtypes = [_u8p, ctypes.c_uint64, _f32p]
 
 
 def _need():
@@ -159,6 +163,51 @@ def dequant(tiles, N, K, decode="ieee"):
     W = np.empty((N, K), np.float32)
     lib.q4o_dequant(_p(t, _u8p), N, K, _p(W, _f32p), _mode(decode))
     return W
+
+
+def q4k_dequant(blocks, N, K, decode="ieee"):
+    """Q4_K rows -> dense f32 W[N, K] (q4rdna_cpu_experiment.cpp:112-135)."""
+    _need()
+    t = _c(blocks, np.uint8).reshape(-1)
+    W = np.empty((N, K), np.float32)
+    lib.q4o_q4k_dequant(_p(t, _u8p), N, K, _p(W, _f32p), _mode(decode))
+    return W
+
+
+def q4k_gemv_f32(blocks, x, N, K, threads=1, decode="ieee"):
+    """The reference Q4_K kernel's f32 order (q4rdna_gemv_bench.hip:93-135).
+    x: [B, K]; returns [B, N]."""
+    _need()
+    t = _c(blocks, np.uint8).reshape(-1)
+    xv = _c(x, np.float32).reshape(-1, K)
+    B = xv.shape[0]
+    y = np.empty((B, N), np.float32)
+    lib.q4o_q4k_gemv_f32(_p(t, _u8p), _p(xv, _f32p), _p(y, _f32p), N, K, B, threads, _mode(decode))
+    return y
+
+
+def q4k_gemv_f64(blocks, x, N, K, threads=1, decode="ieee"):
+    """fp64-accumulated y over the dequantised Q4_K weights, and sum |W x|."""
+    _need()
+    t = _c(blocks, np.uint8).reshape(-1)
+    xv = _c(x, np.float32).reshape(-1, K)
+    B = xv.shape[0]
+    y = np.empty((B, N), np.float64)
+    mag = np.empty((B, N), np.float64)
+    lib.q4o_q4k_gemv_f64(_p(t, _u8p), _p(xv, _f32p), _p(y, _f64p), _p(mag, _f64p), N, K, B, threads, _mode(decode))
+    return y, mag
+
+
+def ref_q4k_dequant(blocks):
+    """The reference's own dequantize_q4_k over consecutive blocks (compiled
+    from q4rdna_cpu_experiment.cpp where it lies) -> f32 [nblocks * 256]."""
+    if ref is None:
+        raise RuntimeError("oracle/_ref/libq4ref.so is not built")
+    t = _c(blocks, np.uint8).reshape(-1)
+    n = t.size // 144
+    out = np.empty(n * 256, np.float32)
+    ref.q4ref_exp_dequant_q4k(_p(t, _u8p), n, _p(out, _f32p))
+    return out
 
 
 def pack_bf16(bf16, threads=1):

@@ -294,3 +294,126 @@ void q4o_pack_bf16(const uint16_t *bf16, int64_t N, int64_t K, uint8_t *tiles, i
         }
     }
 }
+
+/* ---- Q4_K: the tensors the reference leaves on llama.cpp's stock path ----
+ * The qkv-fallback scope (source/q4rdna.cu:685-691) keeps the Q/K/V
+ * projections in ggml's block_q4_K format, and the reference bench times a
+ * Q4_K GEMV beside its own (q4rdna_gemv_bench.hip:93-135).  A block holds 256
+ * weights of one row in 144 bytes (q4rdna_cpu_experiment.cpp:17,
+ * q4rdna_gemv_bench.hip:25-26):
+ *   bytes 0-1   fp16 d, bytes 2-3 fp16 dmin;
+ *   bytes 4-15  eight 6-bit scales and eight 6-bit mins (q4k_scale_min);
+ *   bytes 16-143 quants: byte 16 + 32c + i holds weight 64c + i in its low
+ *               nibble and weight 64c + 32 + i in its high nibble (unsigned).
+ * weight = (d * scale_j) * q - dmin * min_j for sub-block j = k / 32.
+ * A row is K / 256 consecutive blocks; rows are consecutive. */
+#define Q4O_QK 256
+#define Q4O_QK_BYTES 144
+
+/* q4rdna_cpu_experiment.cpp:102-110 (get_scale_min; the bench's copy is the same). */
+static void q4k_scale_min(int j, const uint8_t *s, int *sc, int *mn) {
+    if (j < 4) {
+        *sc = s[j] & 63;
+        *mn = s[j + 4] & 63;
+    } else {
+        *sc = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4);
+        *mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+
+static inline float q4k_half(const uint8_t *p, int ieee) {
+    uint16_t h; memcpy(&h, p, 2);
+    return ieee ? q4o_fp16_to_f32_ieee(h) : q4o_fp16_to_f32(h);
+}
+
+/* Dense W[N][K] from Q4_K rows, q4rdna_cpu_experiment.cpp:112-135: per
+ * chunk c, weight 64c + i = d*scale0*float(q & 15) - dmin*min0 and weight
+ * 64c + 32 + i = d*scale1*float(q >> 4) - dmin*min1, evaluated left to right
+ * in f32 (d*scale*q is exact, so the subtraction is the only rounding). */
+void q4o_q4k_dequant(const uint8_t *blocks, int64_t N, int64_t K, float *W, int ieee) {
+    const int64_t nb = K / Q4O_QK;
+    for (int64_t row = 0; row < N; ++row)
+        for (int64_t b = 0; b < nb; ++b) {
+            const uint8_t *blk = blocks + (uint64_t)(row * nb + b) * Q4O_QK_BYTES;
+            const float d = q4k_half(blk, ieee), dmin = q4k_half(blk + 2, ieee);
+            float *w = W + row * K + b * Q4O_QK;
+            for (int c = 0; c < 4; ++c) {
+                int s0, m0, s1, m1;
+                q4k_scale_min(2 * c, blk + 4, &s0, &m0);
+                q4k_scale_min(2 * c + 1, blk + 4, &s1, &m1);
+                for (int i = 0; i < 32; ++i) {
+                    const uint8_t p = blk[16 + 32 * c + i];
+                    w[64 * c + i] = d * (float)s0 * (float)(p & 15) - dmin * (float)m0;
+                    w[64 * c + 32 + i] = d * (float)s1 * (float)(p >> 4) - dmin * (float)m1;
+                }
+            }
+        }
+}
+
+/* One row of the reference's Q4_K GEMV in its f32 order
+ * (q4rdna_gemv_bench.hip:93-135, one lane per row): blocks ascending, chunks
+ * ascending, i ascending; ds = d*scale, dm = dmin*min per sub-block;
+ * sum = fmaf(ds0*q_lo - dm0, x[64c+i], sum); sum = fmaf(ds1*q_hi - dm1,
+ * x[64c+32+i], sum).  ds*q is exact, so contracting ds*q - dm into one fma
+ * (as a GPU compiler may) gives the same weight. */
+static float q4k_row_f32(const uint8_t *row_blocks, int64_t nb, const float *x, int ieee) {
+    float sum = 0.0f;
+    for (int64_t b = 0; b < nb; ++b) {
+        const uint8_t *blk = row_blocks + (uint64_t)b * Q4O_QK_BYTES;
+        const float d = q4k_half(blk, ieee), dmin = q4k_half(blk + 2, ieee);
+        const float *xb = x + b * Q4O_QK;
+        for (int c = 0; c < 4; ++c) {
+            int s0, m0, s1, m1;
+            q4k_scale_min(2 * c, blk + 4, &s0, &m0);
+            q4k_scale_min(2 * c + 1, blk + 4, &s1, &m1);
+            const float ds0 = d * (float)s0, dm0 = dmin * (float)m0;
+            const float ds1 = d * (float)s1, dm1 = dmin * (float)m1;
+            for (int i = 0; i < 32; ++i) {
+                const uint8_t p = blk[16 + 32 * c + i];
+                const float w0 = ds0 * (float)(p & 15) - dm0;
+                const float w1 = ds1 * (float)(p >> 4) - dm1;
+                sum = fmaf(w0, xb[64 * c + i], sum);
+                sum = fmaf(w1, xb[64 * c + 32 + i], sum);
+            }
+        }
+    }
+    return sum;
+}
+
+/* y[b][n] in the reference Q4_K kernel's order, B columns x[b*K + k]. */
+void q4o_q4k_gemv_f32(const uint8_t *blocks, const float *x, float *y,
+                      int64_t N, int64_t K, int64_t B, int threads, int ieee) {
+    const int64_t nb = K / Q4O_QK;
+#pragma omp parallel for schedule(static) num_threads(threads > 0 ? threads : 1) if (threads > 1)
+    for (int64_t row = 0; row < N; ++row)
+        for (int64_t b = 0; b < B; ++b)
+            y[b * N + row] = q4k_row_f32(blocks + (uint64_t)row * nb * Q4O_QK_BYTES, nb, x + b * K, ieee);
+}
+
+/* fp64-accumulated y over the dequantised weights (q4o_q4k_dequant's values)
+ * and the per-row sum |W x|: the accuracy yardstick, as q4o_gemv_f64. */
+void q4o_q4k_gemv_f64(const uint8_t *blocks, const float *x, double *y, double *absdot,
+                      int64_t N, int64_t K, int64_t B, int threads, int ieee) {
+    const int64_t nb = K / Q4O_QK;
+#pragma omp parallel for schedule(static) num_threads(threads > 0 ? threads : 1) if (threads > 1)
+    for (int64_t row = 0; row < N; ++row) {
+        float w[Q4O_QK];
+        for (int64_t b = 0; b < B; ++b) {
+            y[b * N + row] = 0.0;
+            if (absdot) absdot[b * N + row] = 0.0;
+        }
+        for (int64_t k0 = 0; k0 < nb; ++k0) {
+            q4o_q4k_dequant(blocks + (uint64_t)(row * nb + k0) * Q4O_QK_BYTES, 1, Q4O_QK, w, ieee);
+            for (int64_t b = 0; b < B; ++b) {
+                const float *xb = x + b * K + k0 * Q4O_QK;
+                double sum = 0.0, mag = 0.0;
+                for (int i = 0; i < Q4O_QK; ++i) {
+                    const double a = (double)w[i] * (double)xb[i];
+                    sum += a; mag += fabs(a);
+                }
+                y[b * N + row] += sum;
+                if (absdot) absdot[b * N + row] += mag;
+            }
+        }
+    }
+}

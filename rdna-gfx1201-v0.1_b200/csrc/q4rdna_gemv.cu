@@ -49,6 +49,7 @@
 #include <vector>
 
 #include "q4rdna.h"
+#include "q4rdna_q4k.h"
 #include "q4rdna_tile.h"
 
 namespace q4 {
@@ -903,6 +904,11 @@ struct q4rdna_plan {
     GatherSignal sig{};
     uint32_t epoch = 0;
     bool gather = false;
+    // Q4_K descriptors (format Q4RDNA_FORMAT_Q4K): their own task table and
+    // launch, after the Q4_RDNA launch on the same stream
+    std::vector<q4k::Task> q4k_host;
+    q4k::Task *q4k_table = nullptr;
+    long long q4k_items = 0;
 };
 
 namespace {
@@ -996,7 +1002,7 @@ q4rdna_status q4rdna_dequant_f32(const uint8_t *tiles, float *W, int N, int K, q
     return Q4RDNA_OK;
 }
 
-q4rdna_status q4rdna_plan_create(const q4rdna_gemv_desc *descs, int count, int B, q4rdna_plan **out) {
+q4rdna_status plan_create_rdna(const q4rdna_gemv_desc *descs, int count, int B, q4rdna_plan **out) {
     if (out == nullptr || descs == nullptr || count <= 0) return Q4RDNA_ERR_INVALID_ARGUMENT;
     *out = nullptr;
     if (B < 1 || B > Q4RDNA_MAX_BATCH) return Q4RDNA_ERR_UNSUPPORTED;
@@ -1084,6 +1090,67 @@ q4rdna_status q4rdna_plan_create(const q4rdna_gemv_desc *descs, int count, int B
     return Q4RDNA_OK;
 }
 
+// Plans with Q4_K descriptors: the Q4_RDNA ones go through plan_create_rdna
+// (in their original order), the Q4_K ones get their own task table.
+q4rdna_status q4rdna_plan_create(const q4rdna_gemv_desc *descs, int count, int B, q4rdna_plan **out) {
+    if (out == nullptr || descs == nullptr || count <= 0) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    std::vector<q4rdna_gemv_desc> rd;
+    std::vector<q4k::Task> kt;
+    long long kitems = 0;
+    uint64_t kw = 0, ka = 0;
+    for (int i = 0; i < count; ++i) {
+        const q4rdna_gemv_desc &e = descs[i];
+        if (e.format == Q4RDNA_FORMAT_Q4RDNA) {
+            rd.push_back(e);
+        } else if (e.format == Q4RDNA_FORMAT_Q4K) {
+            q4k::Task T;
+            long long items = 0;
+            const q4rdna_status st = q4k_build_task(e, B, kitems, T, items);
+            if (st != Q4RDNA_OK) return st;
+            kt.push_back(T);
+            kitems += items;
+            const uint64_t w = q4rdna_q4k_bytes(e.N, e.K);
+            kw += w;
+            ka += w + 4ull * e.K * B + 4ull * e.N * B + (e.op == Q4RDNA_OP_ADD ? 4ull * e.N * B : 0ull);
+        } else {
+            return Q4RDNA_ERR_INVALID_ARGUMENT;
+        }
+    }
+    if (B < 1 || B > Q4RDNA_MAX_BATCH) return Q4RDNA_ERR_UNSUPPORTED;
+    q4rdna_plan *p = nullptr;
+    if (!rd.empty()) {
+        const q4rdna_status st = plan_create_rdna(rd.data(), (int)rd.size(), B, &p);
+        if (st != Q4RDNA_OK) return st;
+    } else {
+        p = new (std::nothrow) q4rdna_plan();
+        if (p == nullptr) return Q4RDNA_ERR_CUDA;
+        cudaGetDevice(&p->device);
+        p->count = 0; p->B = B; p->nb = B;
+    }
+    if (!kt.empty()) {
+        if (cudaMalloc(&p->q4k_table, sizeof(q4k::Task) * kt.size()) != cudaSuccess ||
+            cudaMemcpy(p->q4k_table, kt.data(), sizeof(q4k::Task) * kt.size(), cudaMemcpyHostToDevice) !=
+                cudaSuccess) {
+            q4rdna_plan_destroy(p);
+            return Q4RDNA_ERR_CUDA;
+        }
+        p->q4k_host = kt;
+        p->q4k_items = kitems;
+        p->weight_bytes += kw;
+        p->algo_bytes += ka;
+    }
+    *out = p;
+    return Q4RDNA_OK;
+}
+
+namespace {
+q4rdna_status launch_q4k(q4rdna_plan *plan, cudaStream_t stream) {
+    if (plan->q4k_host.empty()) return Q4RDNA_OK;
+    return q4k_launch_tasks(plan->q4k_table, nullptr, (int)plan->q4k_host.size(), plan->B, plan->q4k_items, stream);
+}
+}  // namespace
+
 q4rdna_status q4rdna_plan_run(q4rdna_plan *plan, q4rdna_stream_t stream) {
     if (plan == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
     int dev = -1;
@@ -1098,13 +1165,19 @@ q4rdna_status q4rdna_plan_run(q4rdna_plan *plan, q4rdna_stream_t stream) {
         }
     }
     if (!plan->gather) {
-        if (segmented) return launch_segments(plan, (cudaStream_t)stream, nullptr, nullptr, nullptr, nullptr);
-        Launch L{};
-        L.table = plan->table;
-        L.ntasks = plan->count;
-        L.B = plan->B;
-        L.total_items = plan->items;
-        return launch(L, plan->grid, plan->nb, plan->dual, (cudaStream_t)stream, plan->norm);
+        q4rdna_status st = Q4RDNA_OK;
+        if (segmented) {
+            st = launch_segments(plan, (cudaStream_t)stream, nullptr, nullptr, nullptr, nullptr);
+        } else if (plan->count > 0) {
+            Launch L{};
+            L.table = plan->table;
+            L.ntasks = plan->count;
+            L.B = plan->B;
+            L.total_items = plan->items;
+            st = launch(L, plan->grid, plan->nb, plan->dual, (cudaStream_t)stream, plan->norm);
+        }
+        if (st != Q4RDNA_OK) return st;
+        return launch_q4k(plan, (cudaStream_t)stream);
     }
     const uint32_t epoch = plan->epoch + 1;
     q4rdna_status st;
@@ -1138,6 +1211,7 @@ q4rdna_status q4rdna_plan_set_gather(q4rdna_plan *plan, int world, int rank, con
         return Q4RDNA_ERR_INVALID_ARGUMENT;
     if (world < 2 || world > kMaxMirrors || rank < 0 || rank >= world || plan->gather)
         return Q4RDNA_ERR_INVALID_ARGUMENT;
+    if (!plan->q4k_host.empty() || plan->count == 0) return Q4RDNA_ERR_UNSUPPORTED;
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev != plan->device) return Q4RDNA_ERR_DEVICE;
     for (int p = 0; p < world; ++p)
@@ -1339,6 +1413,17 @@ q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *
     if (plan->gather) return Q4RDNA_ERR_UNSUPPORTED;
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev != plan->device) return Q4RDNA_ERR_DEVICE;
+    if (!plan->q4k_host.empty()) {
+        // plans with Q4_K tensors: one copy in, the run, one copy out (not overlapped)
+        cudaStream_t cs = (cudaStream_t)stream;
+        if (cudaMemcpyAsync(x_dev, x_host, x_bytes, cudaMemcpyHostToDevice, cs) != cudaSuccess)
+            return Q4RDNA_ERR_CUDA;
+        const q4rdna_status st = q4rdna_plan_run(plan, stream);
+        if (st != Q4RDNA_OK) return st;
+        if (cudaMemcpyAsync(y_host, y_dev, y_bytes, cudaMemcpyDeviceToHost, cs) != cudaSuccess)
+            return Q4RDNA_ERR_CUDA;
+        return Q4RDNA_OK;
+    }
     const int want = segments == 0 ? kHostSegments : segments;
     if (plan->seg_request != std::max(1, std::min(want, plan->count)) || plan->seg_x != x_dev ||
         plan->seg_y != y_dev) {
@@ -1402,9 +1487,9 @@ q4rdna_status q4rdna_ipc_free(void *dev_ptr) {
 
 q4rdna_status q4rdna_plan_get_info(const q4rdna_plan *plan, q4rdna_plan_info *info) {
     if (plan == nullptr || info == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
-    info->count = plan->count;
+    info->count = plan->count + (int)plan->q4k_host.size();
     info->batch = plan->B;
-    info->items = plan->items;
+    info->items = plan->items + plan->q4k_items;
     info->grid = plan->grid;
     info->weight_bytes = plan->weight_bytes;
     info->algo_bytes = plan->algo_bytes;
@@ -1415,6 +1500,7 @@ q4rdna_status q4rdna_plan_get_info(const q4rdna_plan *plan, q4rdna_plan_info *in
 void q4rdna_plan_destroy(q4rdna_plan *plan) {
     if (plan == nullptr) return;
     if (plan->table) cudaFree(plan->table);
+    if (plan->q4k_table) cudaFree(plan->q4k_table);
     for (auto &sg : plan->segs) {
         if (sg.table) cudaFree(sg.table);
         for (Task *t : sg.gtable)
@@ -1434,7 +1520,7 @@ void q4rdna_plan_destroy(q4rdna_plan *plan) {
     delete plan;
 }
 
-uint64_t q4rdna_launch_count(void) { return g_launches.load(); }
+uint64_t q4rdna_launch_count(void) { return g_launches.load() + q4k_launch_count(); }
 
 uint32_t q4rdna_take_fault(void) {
     unsigned v = 0, zero = 0;

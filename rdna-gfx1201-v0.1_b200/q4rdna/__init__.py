@@ -22,6 +22,8 @@ LIB_PATH = os.path.join(_HERE, "libq4rdna.so")
 
 OK = 0
 OP_PLAIN, OP_ADD, OP_SWIGLU = 0, 1, 2
+FORMAT_Q4RDNA, FORMAT_Q4K = 0, 1
+Q4K_BLOCK, Q4K_BLOCK_BYTES = 256, 144
 MAX_BATCH = 16
 STATUS = {
     0: "OK", 1: "INVALID_ARGUMENT", 2: "SHAPE", 3: "ALIGNMENT", 4: "WORKSPACE", 5: "UNSUPPORTED",
@@ -42,7 +44,7 @@ class Cfg(ctypes.Structure):
 class GemvDesc(ctypes.Structure):
     _fields_ = [("tiles", c_void_p), ("gate_tiles", c_void_p), ("x", c_void_p), ("add", c_void_p),
                 ("y", c_void_p), ("N", c_int), ("K", c_int), ("op", c_int), ("split", c_int),
-                ("norm_weight", c_void_p), ("norm_eps", ctypes.c_float)]
+                ("norm_weight", c_void_p), ("norm_eps", ctypes.c_float), ("format", c_int)]
 
 
 class PlanInfo(ctypes.Structure):
@@ -65,6 +67,9 @@ def _bind(lib):
         "q4rdna_gemv_rmsnorm": (c_int, [P, P, P, P, ctypes.c_float, P, P, c_int, c_int, c_int, c_int, POINTER(Cfg), P,
                                         c_size_t, P]),
         "q4rdna_pack_bf16": (c_int, [P, P, c_int, c_int, P]),
+        "q4rdna_q4k_bytes": (c_size_t, [c_int, c_int]),
+        "q4rdna_q4k_gemv": (c_int, [P, P, P, P, c_int, c_int, c_int, P]),
+        "q4rdna_q4k_dequant_f32": (c_int, [P, P, c_int, c_int, P]),
         "q4rdna_gemv_noalloc": (c_int, [P, P, P, c_int, c_int, c_int, POINTER(Cfg), P]),
         "q4rdna_plan_create": (c_int, [POINTER(GemvDesc), c_int, c_int, POINTER(P)]),
         "q4rdna_plan_run": (c_int, [P, P]),
@@ -106,6 +111,7 @@ SYMBOLS = [
     "q4rdna_workspace_init", "q4rdna_gemv", "q4rdna_gemv_add", "q4rdna_gemv_swiglu", "q4rdna_dequant_f32", "q4rdna_pack_bf16",
     "q4rdna_gemv_rmsnorm",
     "q4rdna_gemv_noalloc",
+    "q4rdna_q4k_bytes", "q4rdna_q4k_gemv", "q4rdna_q4k_dequant_f32",
     "q4rdna_plan_create", "q4rdna_plan_run", "q4rdna_plan_get_info", "q4rdna_plan_destroy",
     "q4rdna_plan_run_host", "q4rdna_plan_set_segments", "q4rdna_plan_set_gather", "q4rdna_plan_gather_parity", "q4rdna_ipc_alloc", "q4rdna_ipc_open",
     "q4rdna_ipc_close", "q4rdna_ipc_free",
@@ -230,6 +236,41 @@ def gemv(tiles, x, *, op: int = OP_PLAIN, add=None, gate_tiles=None, out=None, s
     return out.reshape(-1) if squeeze else out
 
 
+def _q4k_rows(blocks, K: int) -> int:
+    if K <= 0 or K % Q4K_BLOCK:
+        raise ValueError("Q4_K needs K % 256 == 0")
+    row = (K // Q4K_BLOCK) * Q4K_BLOCK_BYTES
+    if blocks.numel() % row:
+        raise ValueError("Q4_K buffer size does not match K")
+    return blocks.numel() // row
+
+
+def q4k_gemv(blocks, x, *, add=None, out=None, stream=None):
+    """y = W x (+ add) for a Q4_K tensor (ggml block_q4_K rows, uint8 CUDA
+    tensor); x f32 [B, K] or [K], add f32 [B, N].  Returns f32 [B, N] (or [N])."""
+    import torch
+
+    squeeze = x.dim() == 1
+    x2 = x.reshape(1, -1) if squeeze else x
+    B, K = x2.shape
+    N = _q4k_rows(blocks, K)
+    if out is None:
+        out = torch.empty((B, N), dtype=torch.float32, device=x.device)
+    rc = _lib().q4rdna_q4k_gemv(blocks.data_ptr(), x2.data_ptr(), add.data_ptr() if add is not None else None,
+                                out.data_ptr(), N, K, B, _stream_handle(stream))
+    check(rc, f"q4k_gemv N={N} K={K} B={B}")
+    return out.reshape(-1) if squeeze else out
+
+
+def q4k_dequant(blocks, N: int, K: int, stream=None):
+    import torch
+
+    W = torch.empty((N, K), dtype=torch.float32, device=blocks.device)
+    check(_lib().q4rdna_q4k_dequant_f32(blocks.data_ptr(), W.data_ptr(), N, K, _stream_handle(stream)),
+          "q4k_dequant")
+    return W
+
+
 def dequant(tiles, N: int, K: int, stream=None):
     import torch
 
@@ -274,8 +315,9 @@ class Plan:
 
     ``descs``: list of dicts with keys tiles, x, y (torch CUDA tensors) and
     optional op, add, gate_tiles, split, norm_weight, norm_eps (fused RMSNorm:
-    x is then the raw hidden state).  The tensors must stay alive; x may
-    be rewritten in place between runs.
+    x is then the raw hidden state) and format (FORMAT_Q4RDNA, the default, or
+    FORMAT_Q4K: ``tiles`` then holds ggml block_q4_K rows).  The tensors must
+    stay alive; x may be rewritten in place between runs.
     """
 
     def __init__(self, descs, B: int = 1):
@@ -288,7 +330,9 @@ class Plan:
             arr[i].x = d["x"].data_ptr()
             arr[i].add = d["add"].data_ptr() if d.get("add") is not None else None
             arr[i].y = d["y"].data_ptr()
-            arr[i].N = _rows(d["tiles"], K)
+            fmt = d.get("format", FORMAT_Q4RDNA)
+            arr[i].format = fmt
+            arr[i].N = _q4k_rows(d["tiles"], K) if fmt == FORMAT_Q4K else _rows(d["tiles"], K)
             arr[i].K = K
             arr[i].op = d.get("op", OP_PLAIN)
             arr[i].split = d.get("split", 0)

@@ -76,3 +76,43 @@ def tiles_torch(N: int, K: int, seed: int, device):
     sc = (torch.randn((T, TILE_ROWS), generator=g, device=device).abs_() * 0.003).to(torch.float16)
     t[:, :64] = sc.view(torch.uint8)
     return t.reshape(-1)
+
+
+# ---- Q4_K (ggml block_q4_K) rows: the format of the Q/K/V tensors that the
+# reference's qkv-fallback scope leaves on llama.cpp's stock path ----
+Q4K_BLOCK = 256
+Q4K_BLOCK_BYTES = 144
+
+
+def q4k_bytes(N: int, K: int) -> int:
+    if K % Q4K_BLOCK:
+        raise ValueError("K % 256 must be 0")
+    return N * (K // Q4K_BLOCK) * Q4K_BLOCK_BYTES
+
+
+def q4k_np(N: int, K: int, seed: int) -> np.ndarray:
+    """Q4_K rows (uint8, N*K/256*144 bytes) from PCG64(seed): uniform quant
+    and 6-bit scale/min bytes; d and dmin = fp16((0.5 + |N(0,1)|) * 2e-4), so
+    that a weight step d * scale spans the Q4_RDNA scales' range (fp16
+    normal; subnormal d and dmin are edge cases of their own)."""
+    nb = N * (K // Q4K_BLOCK) if K % Q4K_BLOCK == 0 else None
+    if nb is None:
+        raise ValueError("K % 256 must be 0")
+    rng = np.random.default_rng(seed)
+    b = rng.integers(0, 256, (nb, Q4K_BLOCK_BYTES), dtype=np.uint8)
+    dd = ((0.5 + np.abs(rng.standard_normal((nb, 2)))) * 2e-4).astype(np.float16)
+    b[:, :4] = dd.view(np.uint8)
+    return b.reshape(-1)
+
+
+def q4k_torch(N: int, K: int, seed: int, device):
+    """Same distributions drawn on the device (not bit-identical to q4k_np)."""
+    import torch
+
+    nb = N * (K // Q4K_BLOCK)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    b = torch.randint(0, 256, (nb, Q4K_BLOCK_BYTES), generator=g, device=device, dtype=torch.uint8)
+    dd = ((torch.randn((nb, 2), generator=g, device=device).abs_() + 0.5) * 2e-4).to(torch.float16)
+    b[:, :4] = dd.view(torch.uint8)
+    return b.reshape(-1)

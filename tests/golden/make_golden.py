@@ -21,6 +21,12 @@ Runs only where the reference checkout and oracle/_ref (built by
 * ref_fp16.json: sha256 of the reference fp16->f32 table over all 65536
   patterns (q4rdna_cpu_experiment.cpp:39-60) and of f32->fp16 on 2^20 seeded
   floats plus edge cases (q4rdna_cpu_experiment.cpp:62-100).
+* ref_q4k_dequant.npz: the reference's Q4_K block dequantiser
+  (dequantize_q4_k, q4rdna_cpu_experiment.cpp:112-135, compiled from the file)
+  on Q4_K blocks from q4rdna.synth.q4k_np plus edge blocks (q4k_blocks()):
+  the blocks and their 256 f32 weights each.
+
+`python make_golden.py` writes all of them; `--only q4k` only the last.
 """
 from __future__ import annotations
 
@@ -70,8 +76,36 @@ def ref_python_packer():
     return mod
 
 
+def q4k_blocks() -> np.ndarray:
+    """64 seeded Q4_K blocks (4 rows x 4096 columns) and 8 edge blocks: zero
+    d and dmin, fp16-subnormal d and dmin, all scale/min bytes 0xFF, negative
+    d, d = dmin = 65504, all quant bytes 0x00 / 0xFF."""
+    b = synth.q4k_np(4, 4096, 31).reshape(-1, 144).copy()
+    e = synth.q4k_np(1, 8 * 256, 32).reshape(-1, 144).copy()
+    h = lambda v: np.array([v], np.float16).view(np.uint8)  # noqa: E731
+    e[0, :4] = 0
+    e[1, 0:2], e[1, 2:4] = h(3e-6), h(1e-7)
+    e[2, 4:16] = 0xFF
+    e[3, 0:2] = h(-0.002)
+    e[4, 0:2], e[4, 2:4] = h(65504.0), h(65504.0)
+    e[5, 16:] = 0x00
+    e[6, 16:] = 0xFF
+    e[7, 4:16] = np.arange(12, dtype=np.uint8) * 21
+    return np.concatenate([b, e]).reshape(-1)
+
+
+def write_q4k():
+    blocks = q4k_blocks()
+    w = oracle.ref_q4k_dequant(blocks)
+    np.savez_compressed(os.path.join(HERE, "ref_q4k_dequant.npz"), blocks=blocks, weights=w)
+
+
 def main():
     assert oracle.ref is not None and os.path.exists(oracle.REF_PACK_BIN), "build oracle/_ref first"
+    if sys.argv[1:] == ["--only", "q4k"]:
+        write_q4k()
+        print("ref_q4k_dequant.npz written to", HERE)
+        return
     # 1. packers
     mats = {name: bf16_matrix(r, c, s) for name, r, c, s in SMALL}
     np.savez_compressed(os.path.join(HERE, "bf16_inputs.npz"), **{n.replace(".", "_"): m for n, m in mats.items()})
@@ -133,6 +167,8 @@ def main():
                "f32_to_fp16_inputs": "tests/golden/make_golden.py:fp16_inputs()",
                "f32_to_fp16_sha256": sha(to16),
                "packer_cpp_vs_python": packer_notes}, open(os.path.join(HERE, "ref_fp16.json"), "w"), indent=1)
+    # 5. Q4_K dequantiser
+    write_q4k()
     print("golden fixtures written to", HERE)
 
 

@@ -151,3 +151,51 @@ def test_epilogue_oracles():
     sw = oracle.gemv_swiglu_f32(up, gate, x, N, K)
     silu = np.array([oracle.lib.q4o_silu(float(v)) for v in yg.reshape(-1)], np.float32).reshape(yg.shape)
     assert np.array_equal(sw, yu * silu)
+
+
+# ---- Q4_K (the qkv-fallback tensors; q4rdna_cpu_experiment.cpp:102-135) ----
+
+def _q4k_fixture():
+    g = np.load(os.path.join(GOLD, "ref_q4k_dequant.npz"))
+    return g["blocks"], g["weights"]
+
+
+def test_q4k_dequant_matches_reference_golden():
+    """The oracle's restatement, in the reference CPU decoding, equals the
+    reference's dequantize_q4_k bit for bit on the committed blocks (edge blocks
+    included: zero, subnormal, negative and maximal d/dmin, 0xFF scale bytes)."""
+    blocks, w = _q4k_fixture()
+    n = blocks.size // 144
+    assert np.array_equal(blocks, make_golden.q4k_blocks())
+    W = oracle.q4k_dequant(blocks, n, 256, decode="refcpu").reshape(-1)
+    assert np.array_equal(W.view(np.uint32), w.view(np.uint32))
+
+
+@pytest.mark.skipif(oracle.ref is None, reason="oracle/_ref not built")
+def test_q4k_dequant_matches_reference_live():
+    blocks = synth.q4k_np(8, 2048, 77)
+    W = oracle.q4k_dequant(blocks, 8, 2048, decode="refcpu").reshape(-1)
+    assert np.array_equal(W.view(np.uint32), oracle.ref_q4k_dequant(blocks).view(np.uint32))
+
+
+def test_q4k_ieee_decode_differs_only_through_subnormal_d():
+    blocks, _ = _q4k_fixture()
+    n = blocks.size // 144
+    Wr = oracle.q4k_dequant(blocks, n, 256, decode="refcpu")
+    Wi = oracle.q4k_dequant(blocks, n, 256, decode="ieee")
+    dd = blocks.reshape(n, 144)[:, :4].copy().view(np.uint16)
+    subn = ((dd & 0x7C00) == 0) & ((dd & 0x3FF) != 0)
+    same = ~subn.any(axis=1)
+    assert np.array_equal(Wr[same].view(np.uint32), Wi[same].view(np.uint32))
+    assert not np.array_equal(Wr[~same], Wi[~same])  # the subnormal edge block decodes differently
+
+
+def test_q4k_gemv_reference_order_close_to_f64():
+    N, K, B = 96, 1280, 3
+    blocks = synth.q4k_np(N, K, 78)
+    x = synth.x_np(K, B, 79)
+    y32 = oracle.q4k_gemv_f32(blocks, x, N, K)
+    y64, mag = oracle.q4k_gemv_f64(blocks, x, N, K)
+    assert np.max(np.abs(y32 - y64) / mag) < 2e-6
+    W = oracle.q4k_dequant(blocks, N, K).astype(np.float64)
+    assert np.allclose(W @ x.T.astype(np.float64), y64.T, rtol=0, atol=1e-12)
