@@ -213,13 +213,18 @@ void q4rdna_plan_destroy(q4rdna_plan *plan);
  * x_host mirrors it byte for byte; [y_dev, y_dev + y_bytes) must hold every
  * output and y_host receives it byte for byte (pinned host memory lets the
  * copies run asynchronously).  The plan is cut into `segments` runs of
- * consecutive descriptors with about equal weight bytes (0: 3).  Segment s's
+ * consecutive descriptors (0: 3) whose weight bytes are graded, in proportion
+ * to 2^min(s, segments - 1 - s): small runs at both ends.  Segment s's
  * activations are copied in on a library copy stream, its GEMVs wait for that
  * copy only, and its outputs are copied out on a second copy stream as soon
  * as they are written.  Consecutive segments run on two library streams, so a
  * segment starts on the SMs the previous one leaves idle.  Only the first
- * segment's input copy and the last
- * segment's output copy are not hidden behind the weight stream.  The
+ * (smallest) segment's input copy and the last (smallest) segment's output
+ * copy are not hidden behind the weight stream.  The whole sequence is
+ * captured once into a CUDA graph (per set of buffers) and replayed, so a call
+ * costs one graph launch of host time (Q4RDNA_HOST_GRAPH=0: direct launches).
+ * The first call with a given set of buffers does the capture; make it outside
+ * any stream capture of the caller.  The
  * segments' activation ranges must not overlap, nor their output ranges.
  * Ordered after prior work on `stream`; `stream` waits for the last copy.  No
  * synchronisation; calls on one plan must not overlap.  No reference

@@ -842,7 +842,22 @@ __global__ void q4_gather_signal_kernel(const __grid_constant__ GatherSignal a) 
 // as one launch, 705 us as 2, 750 us as 4).  q4rdna_plan_run_host defaults to 3
 // segments, the measured best trade between hidden copies and that cost
 // (e2e 820 us; 856 us with 1 segment, 865 us with 4).
+// q4rdna_plan_run_host's default segment count.  Its segments are graded
+// (weights 1, 2, 1): a segment's activation and output copies take about 0.44
+// of its compute time over PCIe, so the middle segment's copies hide behind
+// the end segments' compute and only the two small end copies show.  More
+// segments cost more than they hide: each launch ends with a tail of idle SMs
+// (Qwen3-8B step, B = 1: e2e 792 us at 3, 959 at 6, 1116 at 8, 1503 at 12).
 constexpr int kHostSegments = 3;
+
+// q4rdna_plan_run_host replays a captured CUDA graph unless Q4RDNA_HOST_GRAPH=0.
+bool host_graph() {
+    static const bool v = [] {
+        const char *e = std::getenv("Q4RDNA_HOST_GRAPH");
+        return e == nullptr || std::strcmp(e, "0") != 0;
+    }();
+    return v;
+}
 
 
 // Device copy of a task table in launch order: tasks with the longest items
@@ -893,8 +908,18 @@ struct q4rdna_plan {
     };
     std::vector<Segment> segs;
     int seg_request = -1;
+    bool seg_graded = false;  // segments cut by graded weights (run_host) or equal ones
     int run_segments = 1;  // q4rdna_plan_run: segment launches (1 = one launch, the default)
     const void *seg_x = nullptr, *seg_y = nullptr;
+    // q4rdna_plan_run_host: the whole copy/launch sequence as one CUDA graph,
+    // keyed by the buffers it was captured with (rebuilt when they change)
+    struct HostGraph {
+        const void *xh = nullptr, *xd = nullptr, *yd = nullptr, *yh = nullptr;
+        size_t xb = 0, yb = 0;
+        cudaGraphExec_t exec = nullptr;
+        uint64_t launches = 0;  // kernel launches one replay performs
+    } hg;
+    cudaStream_t cap = nullptr;  // capture stream
     cudaStream_t h2d = nullptr, d2h = nullptr;
     cudaStream_t comp[2] = {nullptr, nullptr};  // segments alternate, so one's tail overlaps the next
     cudaEvent_t start = nullptr, done = nullptr;
@@ -913,7 +938,7 @@ struct q4rdna_plan {
 
 namespace {
 q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t xb, const uint8_t *yd,
-                             size_t yb);
+                             size_t yb, bool graded = false);
 q4rdna_status launch_segments(q4rdna_plan *plan, cudaStream_t cs, const uint8_t *xh, uint8_t *xd, const uint8_t *yd,
                               uint8_t *yh, int par = -1);
 }  // namespace
@@ -1159,7 +1184,7 @@ q4rdna_status q4rdna_plan_run(q4rdna_plan *plan, q4rdna_stream_t stream) {
     const bool segmented = nseg > 1 && plan->count > 1;
     if (segmented) {
         const int want = std::min(nseg, plan->count);
-        if (plan->seg_request != want) {
+        if (plan->seg_request != want || plan->seg_graded) {
             const q4rdna_status st = build_segments(plan, want, nullptr, 0, nullptr, 0);
             if (st != Q4RDNA_OK) return st;
         }
@@ -1256,10 +1281,12 @@ q4rdna_status q4rdna_plan_set_gather(q4rdna_plan *plan, int world, int rank, con
 
 namespace {
 
-// Cuts the plan into `want` runs of consecutive tasks with about equal weight
-// bytes and gives each its own device task table, events and byte ranges.
+// Cuts the plan into `want` runs of consecutive tasks and gives each its own
+// device task table, events and byte ranges.  Equal weight bytes per run, or
+// with `graded` weights 2^min(s, want - 1 - s): small runs at both ends, so
+// that the first input copy and the last output copy are short.
 q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t xb, const uint8_t *yd,
-                             size_t yb) {
+                             size_t yb, bool graded) {
     for (auto &sg : p->segs) {
         if (sg.table) cudaFree(sg.table);
         for (Task *t : sg.gtable)
@@ -1269,17 +1296,27 @@ q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t
     }
     p->segs.clear();
     p->seg_request = -1;
+    if (p->hg.exec) {  // the graph holds the old segments' tables and events
+        cudaGraphExecDestroy(p->hg.exec);
+        p->hg = q4rdna_plan::HostGraph{};
+    }
     DeviceInfo d;
     if (!device_info(d)) return Q4RDNA_ERR_DEVICE;
     const int n = p->count;
     want = std::max(1, std::min(want, n));
     uint64_t total = 0;
     for (const Task &T : p->host) total += (uint64_t)T.N * T.K * (T.op == Q4RDNA_OP_SWIGLU ? 2 : 1);
+    std::vector<double> cum(want);  // cumulative share of the weights after run s
+    double wsum = 0;
+    for (int s = 0; s < want; ++s) {
+        wsum += graded ? std::ldexp(1.0, std::min(std::min(s, want - 1 - s), 30)) : 1.0;
+        cum[s] = wsum;
+    }
     int first = 0;
     uint64_t acc = 0;
     for (int s = 0; s < want && first < n; ++s) {
         int last = first;  // exclusive end
-        const uint64_t goal = total * (uint64_t)(s + 1) / (uint64_t)want;
+        const uint64_t goal = (uint64_t)((double)total * (cum[s] / wsum));
         while (last < n && (last == first || acc < goal || s == want - 1)) {
             const Task &T = p->host[last];
             acc += (uint64_t)T.N * T.K * (T.op == Q4RDNA_OP_SWIGLU ? 2 : 1);
@@ -1334,6 +1371,7 @@ q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t
          cudaEventCreateWithFlags(&p->done, cudaEventDisableTiming) != cudaSuccess))
         return Q4RDNA_ERR_CUDA;
     p->seg_request = want;
+    p->seg_graded = graded;
     p->seg_x = xd;
     p->seg_y = yd;
     return Q4RDNA_OK;
@@ -1425,18 +1463,55 @@ q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *
         return Q4RDNA_OK;
     }
     const int want = segments == 0 ? kHostSegments : segments;
-    if (plan->seg_request != std::max(1, std::min(want, plan->count)) || plan->seg_x != x_dev ||
+    if (plan->seg_request != std::max(1, std::min(want, plan->count)) || !plan->seg_graded || plan->seg_x != x_dev ||
         plan->seg_y != y_dev) {
         const q4rdna_status st = build_segments(plan, want, static_cast<const uint8_t *>(x_dev), x_bytes,
-                                                static_cast<const uint8_t *>(y_dev), y_bytes);
+                                                static_cast<const uint8_t *>(y_dev), y_bytes, true);
         if (st != Q4RDNA_OK) return st;
     } else {
         for (const auto &sg : plan->segs)
             if (sg.x_hi > x_bytes || sg.y_hi > y_bytes) return Q4RDNA_ERR_INVALID_ARGUMENT;
     }
-    return launch_segments(plan, (cudaStream_t)stream, static_cast<const uint8_t *>(x_host),
-                           static_cast<uint8_t *>(x_dev), static_cast<const uint8_t *>(y_dev),
-                           static_cast<uint8_t *>(y_host));
+    if (!host_graph()) {
+        return launch_segments(plan, (cudaStream_t)stream, static_cast<const uint8_t *>(x_host),
+                               static_cast<uint8_t *>(x_dev), static_cast<const uint8_t *>(y_dev),
+                               static_cast<uint8_t *>(y_host));
+    }
+    // One graph replay per call: a plan of S segments issues about 10 S copies,
+    // launches and event operations, which at S = 8 cost more host time than
+    // the GPU needs for the whole step.
+    auto &hg = plan->hg;
+    if (hg.exec == nullptr || hg.xh != x_host || hg.xd != x_dev || hg.yd != y_dev || hg.yh != y_host ||
+        hg.xb != x_bytes || hg.yb != y_bytes) {
+        if (hg.exec) cudaGraphExecDestroy(hg.exec);
+        hg = q4rdna_plan::HostGraph{};
+        if (plan->cap == nullptr && cudaStreamCreateWithFlags(&plan->cap, cudaStreamNonBlocking) != cudaSuccess)
+            return Q4RDNA_ERR_CUDA;
+        if (cudaStreamBeginCapture(plan->cap, cudaStreamCaptureModeRelaxed) != cudaSuccess) return Q4RDNA_ERR_CUDA;
+        const uint64_t before = g_launches.load();
+        const q4rdna_status st = launch_segments(plan, plan->cap, static_cast<const uint8_t *>(x_host),
+                                                 static_cast<uint8_t *>(x_dev), static_cast<const uint8_t *>(y_dev),
+                                                 static_cast<uint8_t *>(y_host));
+        const uint64_t captured = g_launches.load() - before;
+        g_launches.fetch_sub(captured, std::memory_order_relaxed);  // counted per replay below
+        cudaGraph_t g = nullptr;
+        const cudaError_t ec = cudaStreamEndCapture(plan->cap, &g);
+        if (st != Q4RDNA_OK || ec != cudaSuccess || g == nullptr) {
+            if (g) cudaGraphDestroy(g);
+            cudaGetLastError();
+            return st != Q4RDNA_OK ? st : Q4RDNA_ERR_CUDA;
+        }
+        cudaGraphExec_t ex = nullptr;
+        const cudaError_t ei = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        if (ei != cudaSuccess) return Q4RDNA_ERR_CUDA;
+        hg.exec = ex;
+        hg.xh = x_host; hg.xd = x_dev; hg.yd = y_dev; hg.yh = y_host; hg.xb = x_bytes; hg.yb = y_bytes;
+        hg.launches = captured;
+    }
+    if (cudaGraphLaunch(hg.exec, (cudaStream_t)stream) != cudaSuccess) return Q4RDNA_ERR_CUDA;
+    g_launches.fetch_add(hg.launches, std::memory_order_relaxed);
+    return Q4RDNA_OK;
 }
 
 q4rdna_status q4rdna_plan_set_segments(q4rdna_plan *plan, int segments) {
@@ -1499,6 +1574,8 @@ q4rdna_status q4rdna_plan_get_info(const q4rdna_plan *plan, q4rdna_plan_info *in
 
 void q4rdna_plan_destroy(q4rdna_plan *plan) {
     if (plan == nullptr) return;
+    if (plan->hg.exec) cudaGraphExecDestroy(plan->hg.exec);
+    if (plan->cap) cudaStreamDestroy(plan->cap);
     if (plan->table) cudaFree(plan->table);
     if (plan->q4k_table) cudaFree(plan->q4k_table);
     for (auto &sg : plan->segs) {
