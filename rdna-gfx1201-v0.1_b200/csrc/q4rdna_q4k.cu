@@ -270,22 +270,35 @@ __device__ __forceinline__ void prep(Stage &st, const XRegs &v, int t) {
 // j < 2: scale = s[i] & 63, min = s[i + 4] & 63 (i = 2j, 2j + 1);
 // j >= 2: scale = (s[i + 4] & 15) | (s[i - 4] >> 6) << 4,
 //         min = (s[i + 4] >> 4) | (s[i] >> 6) << 4.
-// Both sub-blocks of a lane are adjacent bytes, handled as one 16-bit pair.
+// Both sub-blocks of a lane are adjacent bytes, handled as one 16-bit pair,
+// with lane-constant byte selectors, shifts and masks (no per-lane branch).
 struct ScaleMin {
     float sc0, sc1, m0, m1;
 };
 
-__device__ __forceinline__ ScaleMin scale_min(const uint4 &h, int j) {
-    const int sh = 16 * (j & 1);
-    const uint32_t A = h.y >> sh, Bm = h.z >> sh, C = h.w >> sh;
-    uint32_t sc, mn;
-    if (j < 2) {
-        sc = A & 0x3F3Fu;
-        mn = Bm & 0x3F3Fu;
-    } else {
-        sc = (C & 0x0F0Fu) | ((A >> 2) & 0x3030u);
-        mn = ((C >> 4) & 0x0F0Fu) | ((Bm >> 2) & 0x3030u);
-    }
+struct ScaleSel {
+    uint32_t low;    // prmt selector: the pair's low-part bytes (from h.y / h.z, or from h.w)
+    uint32_t high;   // prmt selector: the pair's bytes s[2jj], s[2jj + 1] of a word
+    uint32_t mask1;  // 0x3F3F (j < 2) or 0x0F0F
+    uint32_t mask2;  // 0 (j < 2) or 0x3030: the two high bits
+    uint32_t mshift; // 0 (j < 2) or 4: mins take the high nibbles of h.w
+};
+
+__device__ __forceinline__ ScaleSel scale_sel(int j) {
+    const uint32_t jj = (uint32_t)(j & 1), lo = j < 2;
+    ScaleSel q;
+    q.high = (2 * jj) | ((2 * jj + 1) << 4);
+    q.low = lo ? q.high : ((4 + 2 * jj) | ((5 + 2 * jj) << 4));
+    q.mask1 = lo ? 0x3F3Fu : 0x0F0Fu;
+    q.mask2 = lo ? 0u : 0x3030u;
+    q.mshift = lo ? 0u : 4u;
+    return q;
+}
+
+__device__ __forceinline__ ScaleMin scale_min(const uint4 &h, const ScaleSel &q) {
+    const uint32_t sc = (__byte_perm(h.y, h.w, q.low) & q.mask1) | ((__byte_perm(h.y, 0u, q.high) >> 2) & q.mask2);
+    const uint32_t mn =
+        ((__byte_perm(h.z, h.w, q.low) >> q.mshift) & q.mask1) | ((__byte_perm(h.z, 0u, q.high) >> 2) & q.mask2);
     ScaleMin r;
     // byte -> 2^23 + byte as a float, minus 2^23: exact
     r.sc0 = __uint_as_float(__byte_perm(sc, 0x4B000000u, 0x7440)) - 8388608.0f;
@@ -326,7 +339,7 @@ __device__ __forceinline__ void load_planes(XPlanes &xp, const Stage &st, int la
 // can be small); the rounding is 2^-24 of each term, a few times
 // 2^-24 sum |w x| for any weights, which stays below the activation rounding
 // of 2^-24 max|x| per sub-block.
-__device__ __forceinline__ float row_dot(const RowRegs &r, const XPlanes &xp, int j) {
+__device__ __forceinline__ float row_dot(const RowRegs &r, const XPlanes &xp, const ScaleSel &ss) {
     const uint32_t q[8] = {r.q0.x, r.q0.y, r.q0.z, r.q0.w, r.q1.x, r.q1.y, r.q1.z, r.q1.w};
     uint32_t a0 = kMagicI, a1 = kMagicI, a2 = kMagicI;  // sub-block 2j, planes 0..2
     uint32_t b0 = kMagicI, b1 = kMagicI, b2 = kMagicI;  // sub-block 2j + 1 (codes x 16)
@@ -345,7 +358,7 @@ __device__ __forceinline__ float row_dot(const RowRegs &r, const XPlanes &xp, in
     const float sb = fmaf(65536.0f, __uint_as_float(b2) - kMagicF,
                           fmaf(256.0f, __uint_as_float(b1) - kMagicF, __uint_as_float(b0) - kMagicF));
     const float2 dd = __half22float2(*reinterpret_cast<const __half2 *>(&r.h.x));  // (d, dmin)
-    const ScaleMin sm = scale_min(r.h, j);
+    const ScaleMin sm = scale_min(r.h, ss);
     float acc = (dd.x * sm.sc0 * xp.u0) * sa;
     acc = fmaf(dd.x * sm.sc1 * xp.u1s, sb, acc);
     acc = fmaf(-(dd.y * sm.m0), xp.xs0, acc);
@@ -388,6 +401,7 @@ __global__ void __launch_bounds__(kThreads, 2) q4k_gemv_kernel(const __grid_cons
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int bo = lane >> 2, j = lane & 3;
     const int wrow = warp * kRowsPerWarp;
+    const ScaleSel ssel = scale_sel(j);
     Cursor cur = cursor_for(L, blockIdx.x);
     if (!cur.valid) return;
     uint4(&ring)[kSlots][kRowChunks] = sm.ring[warp];
@@ -436,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 2) q4k_gemv_kernel(const __grid_cons
             if (i == 0) issue_x(sm.xraw[buf ^ 1], L, nxt, t);
             cp_async_commit();
             slot = slot + 1 < kSlots ? slot + 1 : 0;
-            acc[i] += row_dot(r, xp, j);
+            acc[i] += row_dot(r, xp, ssel);
         }
         if (cur.step + 1 == cur.steps) {
             const Task &T = task_at(L, cur.task);
