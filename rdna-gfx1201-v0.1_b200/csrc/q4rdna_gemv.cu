@@ -1053,6 +1053,29 @@ q4rdna_status plan_create_rdna(const q4rdna_gemv_desc *descs, int count, int B, 
                               kernel_cfg(variant(), B, any_dual_task).warps;
     const double want_items = plan_items_per_worker() * (double)workers;
     const int plan_split = total_rb > 0 ? (int)std::max(1.0, std::ceil(want_items / (double)total_rb)) : 1;
+    // Tail split (Q4RDNA_TAIL_SPLIT = S > 1, A/B measurements): the tasks with
+    // the cheapest items, about one item per worker of them, are split S ways,
+    // so that the plan's last round (items run longest first) is made of
+    // smaller items.
+    std::vector<int> tail_req(count, 0);
+    if (const char *ts = std::getenv("Q4RDNA_TAIL_SPLIT")) {
+        const int S = std::atoi(ts);
+        if (S > 1 && plan_split == 1) {
+            std::vector<int> order(count);
+            for (int i = 0; i < count; ++i) order[i] = i;
+            auto cost = [&](int i) {
+                return (long long)(descs[i].K / Q4_GROUP) * (descs[i].op == Q4RDNA_OP_SWIGLU ? 2 : 1);
+            };
+            std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return cost(a) < cost(b); });
+            long long acc = 0;
+            for (int i : order) {
+                if (acc >= workers) break;
+                if (descs[i].split > 0 || descs[i].N <= 0) continue;
+                tail_req[i] = S;
+                acc += (long long)(descs[i].N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS * S;
+            }
+        }
+    }
     for (int i = 0; i < count; ++i) {
         const q4rdna_gemv_desc &e = descs[i];
         q4rdna_status st = check_shape(e.N, e.K, B);
@@ -1068,7 +1091,7 @@ q4rdna_status plan_create_rdna(const q4rdna_gemv_desc *descs, int count, int B, 
         const int planes = e.op == Q4RDNA_OP_SWIGLU ? 2 : 1;
         const int G = e.K / Q4_GROUP;
         const int RB = (e.N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
-        const int req = e.split > 0 ? e.split : std::min(plan_split, G);
+        const int req = e.split > 0 ? e.split : std::min(tail_req[i] > 0 ? tail_req[i] : plan_split, G);
         const Split sp = make_split(G, req);
         Task &T = host[i];
         T.w = e.tiles; T.w2 = e.gate_tiles; T.x = e.x; T.add = e.add; T.y = e.y;
