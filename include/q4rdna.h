@@ -213,14 +213,20 @@ void q4rdna_plan_destroy(q4rdna_plan *plan);
  * x_host mirrors it byte for byte; [y_dev, y_dev + y_bytes) must hold every
  * output and y_host receives it byte for byte (pinned host memory lets the
  * copies run asynchronously).  The plan is cut into `segments` runs of
- * consecutive descriptors (0: 3) whose weight bytes are graded, in proportion
- * to 2^min(s, segments - 1 - s): small runs at both ends.  Segment s's
+ * consecutive descriptors (0: 2 with direct output stores, see below, else 3)
+ * whose weight bytes are graded, in proportion to 2^min(s, segments - 1 - s):
+ * small runs at both ends.  Segment s's
  * activations are copied in on a library copy stream, its GEMVs wait for that
  * copy only, and its outputs are copied out on a second copy stream as soon
  * as they are written.  Consecutive segments run on two library streams, so a
  * segment starts on the SMs the previous one leaves idle.  Only the first
  * (smallest) segment's input copy and the last (smallest) segment's output
- * copy are not hidden behind the weight stream.  The whole sequence is
+ * copy are not hidden behind the weight stream.  When y_host is pinned host
+ * memory mapped for the device (cudaHostAlloc / cudaMallocHost, or registered
+ * as mapped), the kernels also store their outputs straight into it, so no
+ * output copies remain and the runs grow instead (2^s); a pageable y_host
+ * keeps the output copies (Q4RDNA_HOST_DIRECT=0 forces them).  y_dev receives
+ * the outputs either way.  The whole sequence is
  * captured once into a CUDA graph (per set of buffers) and replayed, so a call
  * costs one graph launch of host time (Q4RDNA_HOST_GRAPH=0: direct launches).
  * The first call with a given set of buffers does the capture; make it outside

@@ -842,13 +842,42 @@ __global__ void q4_gather_signal_kernel(const __grid_constant__ GatherSignal a) 
 // as one launch, 705 us as 2, 750 us as 4).  q4rdna_plan_run_host defaults to 3
 // segments, the measured best trade between hidden copies and that cost
 // (e2e 820 us; 856 us with 1 segment, 865 us with 4).
-// q4rdna_plan_run_host's default segment count.  Its segments are graded
-// (weights 1, 2, 1): a segment's activation and output copies take about 0.44
-// of its compute time over PCIe, so the middle segment's copies hide behind
-// the end segments' compute and only the two small end copies show.  More
-// segments cost more than they hide: each launch ends with a tail of idle SMs
-// (Qwen3-8B step, B = 1: e2e 792 us at 3, 959 at 6, 1116 at 8, 1503 at 12).
+// q4rdna_plan_run_host's default segment counts.  A segment's activation and
+// output copies take about 0.44 of its compute time over PCIe, and each extra
+// launch ends with a tail of idle SMs, so few graded segments win:
+// - output copies: weights 1, 2, 1; the middle segment's copies hide behind
+//   the end segments' compute (Qwen3-8B step, B = 1: e2e 792 us at 3, 959 at
+//   6, 1116 at 8);
+// - outputs stored straight into the host buffer: weights 1, 2; the second
+//   segment's input copy hides behind the first one's compute (712 us at 2,
+//   773 at 3, 843 at 4).
 constexpr int kHostSegments = 3;
+constexpr int kHostSegmentsDirect = 2;
+
+// q4rdna_plan_run_host stores outputs straight into a mapped pinned host
+// buffer unless Q4RDNA_HOST_DIRECT=0.
+bool host_direct() {
+    static const bool v = [] {
+        const char *e = std::getenv("Q4RDNA_HOST_DIRECT");
+        return e == nullptr || std::strcmp(e, "0") != 0;
+    }();
+    return v;
+}
+
+// Device address of run_host's output buffer when the whole [yh, yh + yb) is
+// pinned host memory mapped for the device (both ends map, at the same
+// distance as on the host), else null: the outputs are then copied.
+uint8_t *mapped_output(const void *yh, size_t yb) {
+    if (yh == nullptr || yb == 0 || !host_direct()) return nullptr;
+    void *a = nullptr, *b = nullptr;
+    uint8_t *r = nullptr;
+    if (cudaHostGetDevicePointer(&a, const_cast<void *>(yh), 0) == cudaSuccess &&
+        cudaHostGetDevicePointer(&b, static_cast<uint8_t *>(const_cast<void *>(yh)) + yb - 1, 0) == cudaSuccess &&
+        static_cast<uint8_t *>(b) - static_cast<uint8_t *>(a) == (ptrdiff_t)(yb - 1))
+        r = static_cast<uint8_t *>(a);
+    cudaGetLastError();  // a pageable or unmapped buffer is not an error here
+    return r;
+}
 
 // q4rdna_plan_run_host replays a captured CUDA graph unless Q4RDNA_HOST_GRAPH=0.
 bool host_graph() {
@@ -909,6 +938,8 @@ struct q4rdna_plan {
     std::vector<Segment> segs;
     int seg_request = -1;
     bool seg_graded = false;  // segments cut by graded weights (run_host) or equal ones
+    bool seg_direct = false;  // run_host: outputs stored straight into the mapped host buffer
+    const void *seg_yh = nullptr;
     int run_segments = 1;  // q4rdna_plan_run: segment launches (1 = one launch, the default)
     const void *seg_x = nullptr, *seg_y = nullptr;
     // q4rdna_plan_run_host: the whole copy/launch sequence as one CUDA graph,
@@ -938,7 +969,7 @@ struct q4rdna_plan {
 
 namespace {
 q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t xb, const uint8_t *yd,
-                             size_t yb, bool graded = false);
+                             size_t yb, bool graded = false, const uint8_t *yh = nullptr);
 q4rdna_status launch_segments(q4rdna_plan *plan, cudaStream_t cs, const uint8_t *xh, uint8_t *xd, const uint8_t *yd,
                               uint8_t *yh, int par = -1);
 }  // namespace
@@ -1307,9 +1338,13 @@ namespace {
 // Cuts the plan into `want` runs of consecutive tasks and gives each its own
 // device task table, events and byte ranges.  Equal weight bytes per run, or
 // with `graded` weights 2^min(s, want - 1 - s): small runs at both ends, so
-// that the first input copy and the last output copy are short.
+// that the first input copy and the last output copy are short.  With `yh`
+// (run_host's output buffer) mapped into the device's address space, every
+// task also stores its outputs there (its one mirror), so no output copies
+// remain; the runs then grow 2^s, so each input copy hides behind the
+// previous run's compute.
 q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t xb, const uint8_t *yd,
-                             size_t yb, bool graded) {
+                             size_t yb, bool graded, const uint8_t *yh) {
     for (auto &sg : p->segs) {
         if (sg.table) cudaFree(sg.table);
         for (Task *t : sg.gtable)
@@ -1327,12 +1362,14 @@ q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t
     if (!device_info(d)) return Q4RDNA_ERR_DEVICE;
     const int n = p->count;
     want = std::max(1, std::min(want, n));
+    uint8_t *yh_dev = graded && xd != nullptr ? mapped_output(yh, yb) : nullptr;
+    const bool direct = yh_dev != nullptr;
     uint64_t total = 0;
     for (const Task &T : p->host) total += (uint64_t)T.N * T.K * (T.op == Q4RDNA_OP_SWIGLU ? 2 : 1);
     std::vector<double> cum(want);  // cumulative share of the weights after run s
     double wsum = 0;
     for (int s = 0; s < want; ++s) {
-        wsum += graded ? std::ldexp(1.0, std::min(std::min(s, want - 1 - s), 30)) : 1.0;
+        wsum += !graded ? 1.0 : std::ldexp(1.0, std::min(direct ? s : std::min(s, want - 1 - s), 30));
         cum[s] = wsum;
     }
     int first = 0;
@@ -1361,6 +1398,10 @@ q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t
             sg.x_hi = std::max(sg.x_hi, (size_t)(x - xd) + xn);
             sg.y_lo = std::min(sg.y_lo, (size_t)(y - yd));
             sg.y_hi = std::max(sg.y_hi, (size_t)(y - yd) + yn);
+            if (direct) {
+                T.nmirror = 1;
+                T.mirror[0] = reinterpret_cast<float *>(yh_dev + (y - yd));
+            }
         }
         const long long end = last < n ? p->host[last].item_begin : p->items;
         sg.items = end - base;
@@ -1395,6 +1436,8 @@ q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t
         return Q4RDNA_ERR_CUDA;
     p->seg_request = want;
     p->seg_graded = graded;
+    p->seg_direct = direct;
+    p->seg_yh = yh;
     p->seg_x = xd;
     p->seg_y = yd;
     return Q4RDNA_OK;
@@ -1419,9 +1462,9 @@ q4rdna_status launch_segments(q4rdna_plan *plan, cudaStream_t cs, const uint8_t 
         cudaStreamWaitEvent(plan->comp[0], plan->start, 0) != cudaSuccess ||
         cudaStreamWaitEvent(plan->comp[1], plan->start, 0) != cudaSuccess)
         return Q4RDNA_ERR_CUDA;
-    if (copies && (cudaStreamWaitEvent(plan->h2d, plan->start, 0) != cudaSuccess ||
-                   cudaStreamWaitEvent(plan->d2h, plan->start, 0) != cudaSuccess))
-        return Q4RDNA_ERR_CUDA;
+    const bool out_copies = copies && !plan->seg_direct;  // direct: the kernels store into yh
+    if (copies && cudaStreamWaitEvent(plan->h2d, plan->start, 0) != cudaSuccess) return Q4RDNA_ERR_CUDA;
+    if (out_copies && cudaStreamWaitEvent(plan->d2h, plan->start, 0) != cudaSuccess) return Q4RDNA_ERR_CUDA;
     for (auto &sg : plan->segs) {
         if (!copies) break;
         if (cudaMemcpyAsync(xd + sg.x_lo, xh + sg.x_lo, sg.x_hi - sg.x_lo, cudaMemcpyHostToDevice, plan->h2d) !=
@@ -1443,13 +1486,13 @@ q4rdna_status launch_segments(q4rdna_plan *plan, cudaStream_t cs, const uint8_t 
         const q4rdna_status st = launch(L, sg.grid, plan->nb, plan->dual, c, plan->norm);
         if (st != Q4RDNA_OK) return st;
         if (cudaEventRecord(sg.y_ready, c) != cudaSuccess) return Q4RDNA_ERR_CUDA;
-        if (!copies) continue;
+        if (!out_copies) continue;
         if (cudaStreamWaitEvent(plan->d2h, sg.y_ready, 0) != cudaSuccess ||
             cudaMemcpyAsync(yh + sg.y_lo, yd + sg.y_lo, sg.y_hi - sg.y_lo, cudaMemcpyDeviceToHost, plan->d2h) !=
                 cudaSuccess)
             return Q4RDNA_ERR_CUDA;
     }
-    if (copies) {
+    if (out_copies) {
         if (cudaEventRecord(plan->done, plan->d2h) != cudaSuccess || cudaStreamWaitEvent(cs, plan->done, 0) != cudaSuccess)
             return Q4RDNA_ERR_CUDA;
     } else {
@@ -1485,11 +1528,13 @@ q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *
             return Q4RDNA_ERR_CUDA;
         return Q4RDNA_OK;
     }
-    const int want = segments == 0 ? kHostSegments : segments;
+    const int want =
+        segments != 0 ? segments : (mapped_output(y_host, y_bytes) != nullptr ? kHostSegmentsDirect : kHostSegments);
     if (plan->seg_request != std::max(1, std::min(want, plan->count)) || !plan->seg_graded || plan->seg_x != x_dev ||
-        plan->seg_y != y_dev) {
+        plan->seg_y != y_dev || plan->seg_yh != y_host) {
         const q4rdna_status st = build_segments(plan, want, static_cast<const uint8_t *>(x_dev), x_bytes,
-                                                static_cast<const uint8_t *>(y_dev), y_bytes, true);
+                                                static_cast<const uint8_t *>(y_dev), y_bytes, true,
+                                                static_cast<const uint8_t *>(y_host));
         if (st != Q4RDNA_OK) return st;
     } else {
         for (const auto &sg : plan->segs)

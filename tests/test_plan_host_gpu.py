@@ -90,3 +90,23 @@ def test_segmented_run_equals_one_launch(cuda, B, segments):
     plan.run()
     assert np.array_equal(y_dev.cpu().numpy().view(np.uint32), want)
     plan.close()
+
+
+@pytest.mark.parametrize("B", [1, 4])
+def test_run_host_pageable_output_falls_back_to_copies(cuda, B):
+    """Pinned output buffers receive the outputs straight from the kernels; a
+    pageable one cannot be mapped for the device, so run_host copies into it
+    instead.  Both give exactly the outputs of copy-in, run, copy-out, and a
+    change of output buffer between calls is picked up."""
+    plan, x_dev, y_dev, x_host, y_pinned = _step(cuda, B, 2400 + B)
+    x_dev.copy_(x_host)
+    plan.run()
+    want = y_dev.cpu().numpy().view(np.uint32).copy()
+    y_pageable = torch.empty(y_pinned.numel(), dtype=torch.float32)
+    for y_host in (y_pinned, y_pageable, y_pinned):
+        y_host.fill_(float("nan"))
+        plan.run_host(x_host, x_dev, y_dev, y_host)
+        torch.cuda.current_stream().synchronize()
+        assert np.array_equal(y_host.numpy().view(np.uint32), want)
+        assert np.array_equal(y_dev.cpu().numpy().view(np.uint32), want)
+    plan.close()
