@@ -10,17 +10,20 @@ L2 flush is needed between steps.
 
   value    aggregate HBM GB/s = algorithmic bytes of the step / device time
   e2e      same metric through the public C ABI with pinned HOST buffers: every
-           step copies all 252 activations host->device and all outputs back
-           (q4rdna_plan_run_host: the copies run in segments overlapped with the
-           GEMVs, so only the first segment's input and the last segment's
-           output copies are exposed)
+           step copies all 252 activations host->device and brings all outputs
+           back (q4rdna_plan_run_host: the kernels store the outputs straight
+           into the pinned buffer, and the input copies run in 2 graded
+           segments overlapped with the GEMVs, so only the first segment's
+           input copy is exposed; one CUDA graph replay per step)
   roofline dominant kernel (the plan kernel) vs MEASURED_PEAKS.json hbm_gbs
   cpu_baseline  the reference's own CPU GEMV (reference_q4_rdna compiled from
            its source into oracle/_ref) on the host cores, bounded sample
 
 --gpus N (under torchrun): every tensor's output rows are sharded over the N
-ranks (tensor parallel, rows in multiples of 32) and the y slices are gathered
-with one NCCL all-gather per step; total work is fixed (strong scaling).
+ranks (tensor parallel, rows in multiples of 32) and the y slices are gathered,
+by default inside the plan kernel (P2P stores into every rank's gathered
+buffer, then a flag exchange), or with one NCCL all-gather per step
+(--gather nccl); total work is fixed (strong scaling).
 --impl reference: the reference CPU implementation alone on the host cores.
 """
 from __future__ import annotations
