@@ -224,8 +224,9 @@ void q4rdna_plan_destroy(q4rdna_plan *plan);
  * copy are not hidden behind the weight stream.  When y_host is pinned host
  * memory mapped for the device (cudaHostAlloc / cudaMallocHost, or registered
  * as mapped), the kernels also store their outputs straight into it, so no
- * output copies remain and the runs grow instead (2^s); a pageable y_host
- * keeps the output copies (Q4RDNA_HOST_DIRECT=0 forces them).  y_dev receives
+ * output copies remain and the runs grow instead; a pageable y_host
+ * keeps the output copies (Q4RDNA_HOST_DIRECT=0 forces them); with direct
+ * stores the runs' weight bytes grow as 4^s (Q4RDNA_HOST_GROWTH).  y_dev receives
  * the outputs either way.  The whole sequence is
  * captured once into a CUDA graph (per set of buffers) and replayed, so a call
  * costs one graph launch of host time (Q4RDNA_HOST_GRAPH=0: direct launches).

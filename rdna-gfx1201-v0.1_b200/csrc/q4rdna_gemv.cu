@@ -839,18 +839,17 @@ __global__ void q4_gather_signal_kernel(const __grid_constant__ GatherSignal a) 
 // Segment counts.  Plan runs default to one launch: with the plan-wide split
 // choice the items are large and few per warp, and segment launches that
 // overlap (two streams) leave SMs idle between segments (Qwen3-8B step: 631 us
-// as one launch, 705 us as 2, 750 us as 4).  q4rdna_plan_run_host defaults to 3
-// segments, the measured best trade between hidden copies and that cost
-// (e2e 820 us; 856 us with 1 segment, 865 us with 4).
-// q4rdna_plan_run_host's default segment counts.  A segment's activation and
-// output copies take about 0.44 of its compute time over PCIe, and each extra
-// launch ends with a tail of idle SMs, so few graded segments win:
+// as one launch, 705 us as 2, 750 us as 4).
+// q4rdna_plan_run_host's default segment counts.  A segment's copies over PCIe
+// take a fraction of its compute time (one whole-buffer copy of the step's
+// activations about 0.16), and each extra launch ends with a tail of idle SMs,
+// so few graded segments win:
 // - output copies: weights 1, 2, 1; the middle segment's copies hide behind
 //   the end segments' compute (Qwen3-8B step, B = 1: e2e 792 us at 3, 959 at
 //   6, 1116 at 8);
-// - outputs stored straight into the host buffer: weights 1, 2; the second
-//   segment's input copy hides behind the first one's compute (712 us at 2,
-//   773 at 3, 843 at 4).
+// - outputs stored straight into the host buffer: weights 1, g (host_growth);
+//   the second segment's input copy hides behind the first one's compute
+//   (712 us at 2 segments, 773 at 3, 843 at 4, with g = 2).
 constexpr int kHostSegments = 3;
 constexpr int kHostSegmentsDirect = 2;
 
@@ -860,6 +859,21 @@ bool host_direct() {
     static const bool v = [] {
         const char *e = std::getenv("Q4RDNA_HOST_DIRECT");
         return e == nullptr || std::strcmp(e, "0") != 0;
+    }();
+    return v;
+}
+
+// Growth of consecutive run_host segments with direct outputs (weights g^s):
+// segment s + 1's input copy must hide behind segment s's compute, and a
+// whole-buffer input copy takes about 0.16 of the step's compute, so a larger
+// g shrinks the exposed first copy until the second one stops hiding.
+// Qwen3-8B step, B = 1, 2 segments: e2e - device 80 us at g = 2, 71 at 4, 96
+// at 6.  Q4RDNA_HOST_GROWTH overrides it.
+double host_growth() {
+    static const double v = [] {
+        const char *e = std::getenv("Q4RDNA_HOST_GROWTH");
+        const double g = (e != nullptr && *e != '\0') ? std::atof(e) : 0.0;
+        return g >= 1.0 ? std::min(g, 64.0) : 4.0;
     }();
     return v;
 }
@@ -1369,7 +1383,9 @@ q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t
     std::vector<double> cum(want);  // cumulative share of the weights after run s
     double wsum = 0;
     for (int s = 0; s < want; ++s) {
-        wsum += !graded ? 1.0 : std::ldexp(1.0, std::min(direct ? s : std::min(s, want - 1 - s), 30));
+        wsum += !graded ? 1.0
+                : direct ? std::pow(host_growth(), (double)std::min(s, 30))
+                         : std::ldexp(1.0, std::min(std::min(s, want - 1 - s), 30));
         cum[s] = wsum;
     }
     int first = 0;
