@@ -257,6 +257,223 @@ def run_pack(args):
             "cpu_baseline": cpu, "gpu_launches": q4rdna.launch_count() - l0, "clocks": clk.summary()}
 
 
+# ------------------------------------------------- single drop-in calls
+
+L2_BYTES = 126 * 1024 * 1024
+# The reference's per-kernel medians (results/kernel_profile.json:46,51,56,
+# RX 9070 XT, rocprofv3 trace of the split-K kernels) for the same shapes.
+REF_MEDIAN_US = {"4096x4096": 16.88, "1024x4096": 5.40, "12288x4096 gate+up": 90.24}
+
+
+def _time_graph(launch, n_launch: int, stream, reps: int = 7):
+    """Median device us per launch: n_launch back-to-back launches captured in
+    one CUDA graph on `stream`, replayed `reps` times between CUDA events."""
+    import torch
+
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(n_launch):
+            launch(i)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ts = []
+    for _ in range(reps):
+        e0.record()
+        g.replay()
+        e1.record()
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3 / n_launch)
+    del g
+    return statistics.median(ts)
+
+
+def run_single(args):
+    """us per GEMV through the drop-in entry points, the way llama.cpp drives
+    the reference (one launch per mul_mat node): configs 0 and 1 of the
+    benchmark, plus the fused gate+up pair.  Each timing is `--single-launches`
+    back-to-back calls captured in a CUDA graph and replayed (device time per
+    call, no host overhead), rotating over enough weight copies to cover >= 4x
+    L2 so every call streams its weights from HBM, as the reference's own
+    benchmark rotates copies (q4rdna_gemv_bench.hip:137-161).  Legs:
+      gemv       q4rdna_gemv (raw pointers, caller workspace), split from the
+                 selector and forced to 1..16 (the split sweep);
+      mul_mat    the name-keyed hooks q4rdna_mul_mat / q4rdna_mul_mat_glu on a
+                 sidecar holding the copies (the selector's split)."""
+    import ctypes
+
+    import torch
+
+    import q4rdna
+    from q4rdna import synth
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L = q4rdna.lib
+    if L is None:
+        raise SystemExit("libq4rdna.so not built")
+    peak, peak_kind = hbm_peak()
+    shapes = [("4096x4096", 4096, 4096, q4rdna.OP_PLAIN), ("12288x4096", 12288, 4096, q4rdna.OP_PLAIN),
+              ("4096x12288", 4096, 12288, q4rdna.OP_PLAIN), ("1024x4096", 1024, 4096, q4rdna.OP_PLAIN),
+              ("12288x4096 gate+up", 12288, 4096, q4rdna.OP_SWIGLU)]
+    if args.single_shapes:
+        keep = set(args.single_shapes.split(","))
+        shapes = [s for s in shapes if s[0] in keep]
+    splits = [0] + (list(range(1, 17)) if args.single_sweep else [])
+    cap = torch.cuda.Stream()  # warm-up and capture stream (the hooks keep a workspace per stream)
+    rows = []
+    l0 = q4rdna.launch_count()
+    with ClockSampler(0) as clk:
+        for si, (name, N, K, op) in enumerate(shapes):
+            planes = 2 if op == q4rdna.OP_SWIGLU else 1
+            tb = N * K * 34 // 64
+            copies = max(2, -(-4 * L2_BYTES // (tb * planes)))
+            W = [synth.tiles_torch(N, K, args.seed + 1000 * si + c, dev) for c in range(copies * planes)]
+            x = torch.randn(K, generator=torch.Generator(device=dev).manual_seed(args.seed + si), device=dev)
+            y = torch.empty(N, device=dev)
+            algo = planes * tb + 4 * K + 4 * N
+            if args.single_ncu:
+                for i in range(3):  # three cold calls (distinct copies), no graph
+                    c = i % copies
+                    h = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+                    need = L.q4rdna_workspace_bytes(N, K, 1, op, None)
+                    ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
+                    rc = (L.q4rdna_gemv_swiglu(W[2 * c].data_ptr(), W[2 * c + 1].data_ptr(), x.data_ptr(), y.data_ptr(),
+                                               N, K, 1, None, ws.data_ptr(), need, h) if op == q4rdna.OP_SWIGLU else
+                          L.q4rdna_gemv(W[c].data_ptr(), x.data_ptr(), y.data_ptr(), N, K, 1, None, ws.data_ptr(), need, h))
+                    if rc != 0:
+                        raise RuntimeError(f"{name}: status {rc}")
+                torch.cuda.synchronize()
+                rows.append({"shape": name, "N": N, "K": K, "leg": "ncu", "split": L.q4rdna_select_split(N, K, 1, op),
+                             "selector": True, "us": 0.0, "algo_bytes": algo, "gbs": 0.0, "frac": 0.0})
+                del W
+                continue
+            for split in splits:
+                if split > K // 64:
+                    continue
+                cfg = q4rdna.Cfg()
+                cfg.split = split
+                need = L.q4rdna_workspace_bytes(N, K, 1, op, ctypes.byref(cfg))
+                ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
+                chosen = L.q4rdna_select_split(N, K, 1, op) if split == 0 else split
+
+                def launch(i, cfg=cfg, need=need, ws=ws):
+                    c = i % copies
+                    h = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+                    if op == q4rdna.OP_SWIGLU:
+                        rc = L.q4rdna_gemv_swiglu(W[2 * c].data_ptr(), W[2 * c + 1].data_ptr(), x.data_ptr(),
+                                                  y.data_ptr(), N, K, 1, ctypes.byref(cfg), ws.data_ptr(), need, h)
+                    else:
+                        rc = L.q4rdna_gemv(W[c].data_ptr(), x.data_ptr(), y.data_ptr(), N, K, 1, ctypes.byref(cfg),
+                                           ws.data_ptr(), need, h)
+                    if rc != 0:
+                        raise RuntimeError(f"q4rdna_gemv {name} split {split}: status {rc}")
+
+                with torch.cuda.stream(cap):
+                    for i in range(20):
+                        launch(i)
+                torch.cuda.synchronize()
+                us = _time_graph(launch, args.single_launches, cap)
+                rows.append({"shape": name, "N": N, "K": K, "leg": "gemv", "split": chosen,
+                             "selector": split == 0, "us": round(us, 3), "algo_bytes": algo,
+                             "gbs": round(algo / (us * 1e-6) / 1e9, 1), "frac": round(algo / (us * 1e-6) / 1e9 / peak, 4)})
+                if split == 0:
+                    # the same calls with programmatic dependent launch: each
+                    # call's first weights stream while the previous one ends
+                    cfg.flags = q4rdna.CFG_OVERLAP_PREVIOUS
+                    us = _time_graph(launch, args.single_launches, cap)
+                    cfg.flags = 0
+                    rows.append({"shape": name, "N": N, "K": K, "leg": "gemv_overlap", "split": chosen,
+                                 "selector": True, "us": round(us, 3), "algo_bytes": algo,
+                                 "gbs": round(algo / (us * 1e-6) / 1e9, 1),
+                                 "frac": round(algo / (us * 1e-6) / 1e9 / peak, 4)})
+            if not args.single_no_hook and name in ("4096x4096", "1024x4096", "12288x4096 gate+up"):
+                rows.append(_time_hook(args, name, N, K, op, W, copies, x, y, algo, peak, cap))
+            del W
+            torch.cuda.empty_cache()
+    sel = {r["shape"]: r for r in rows if r["leg"] == "gemv" and r["selector"]}
+    ovl = {r["shape"]: r for r in rows if r["leg"] == "gemv_overlap"}
+    best = {}
+    for r in rows:
+        if r["leg"] == "gemv" and (r["shape"] not in best or r["us"] < best[r["shape"]]["us"]):
+            best[r["shape"]] = r
+    summary = {k: {"us": v["us"], "split": v["split"], "frac": v["frac"], "best_split": best[k]["split"],
+                   "best_us": best[k]["us"], "us_overlapped": ovl[k]["us"] if k in ovl else None,
+                   "reference_median_us": REF_MEDIAN_US.get(k)}
+               for k, v in sel.items()}
+    c0 = sel.get("4096x4096")
+    return {"metric": "us per Q4-g64 GEMV through the drop-in entry points (batch 1), and HBM GB/s",
+            "value": c0["us"] if c0 else None, "unit": "us", "higher_is_better": False, "n_gpus": 1,
+            "dtype": "int4 x f32 (fp16 scales, f32 accumulate)",
+            "data": "synthetic: uniform int4 codes, fp16 scales |N(0,1)|*0.003, x ~ N(0,1) f32",
+            "config": {"workload": "configs 0 and 1: single GEMVs, batch 1, one launch per call",
+                       "launches_per_timing": args.single_launches,
+                       "l2": ">= 4x L2 of rotating weight copies per shape (no flush needed)",
+                       "timing": "CUDA graph of back-to-back calls, CUDA events, median of 7 replays"},
+            "peak": peak, "peak_kind": peak_kind, "summary": summary, "rows": rows,
+            "gpu_launches": q4rdna.launch_count() - l0, "clocks": clk.summary()}
+
+
+def _time_hook(args, name, N, K, op, W, copies, x, y, algo, peak, cap):
+    """The name-keyed hooks on a sidecar that holds the rotating copies."""
+    import ctypes
+
+    import torch
+
+    import q4rdna
+    from q4rdna import format as fmt
+
+    tmp = tempfile.mkdtemp(prefix="q4rdna_single_")
+    path = os.path.join(tmp, "copies.q4rdna")
+    if op == q4rdna.OP_SWIGLU:
+        tensors = []
+        for c in range(copies):
+            tensors.append((f"blk.{c}.ffn_up.weight", W[2 * c].cpu().numpy(), N, K))
+            tensors.append((f"blk.{c}.ffn_gate.weight", W[2 * c + 1].cpu().numpy(), N, K))
+    else:
+        suffix = "attn_output" if N == K else "attn_k"
+        tensors = [(f"blk.{c}.{suffix}.weight", W[c].cpu().numpy(), N, K) for c in range(copies)]
+    fmt.write_sidecar(path, tensors)
+    L = q4rdna.lib
+    q4rdna.registry_reset()
+    os.environ["LLAMA_Q4_RDNA_SIDECAR"] = path
+    os.environ.pop("LLAMA_Q4_RDNA_SCOPE", None)
+    names = [t[0].encode() for t in tensors]
+
+    def launch(i):
+        c = i % copies
+        h = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        if op == q4rdna.OP_SWIGLU:
+            ok = L.q4rdna_mul_mat_glu(names[2 * c], K, N, names[2 * c + 1], K, N, x.data_ptr(), K, y.data_ptr(), N, h)
+        else:
+            ok = L.q4rdna_mul_mat(names[c], K, N, x.data_ptr(), K, y.data_ptr(), N, h)
+        if ok != 1:
+            raise RuntimeError(f"name-keyed hook fell back for {name}")
+
+    with torch.cuda.stream(cap):  # loads the sidecar and this stream's workspace outside the capture
+        for i in range(20):
+            launch(i)
+    torch.cuda.synchronize()
+    us = _time_graph(launch, args.single_launches, cap)
+    # host cost of one hook call (ctypes from Python: an upper bound of the C cost)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(cap):
+        t0 = time.perf_counter()
+        for i in range(200):
+            launch(i)
+        host_us = (time.perf_counter() - t0) / 200 * 1e6
+    torch.cuda.synchronize()
+    q4rdna.registry_reset()
+    os.environ.pop("LLAMA_Q4_RDNA_SIDECAR", None)
+    os.unlink(path)
+    os.rmdir(tmp)
+    split = L.q4rdna_select_split(N, K, 1, op)
+    return {"shape": name, "N": N, "K": K, "leg": "mul_mat_glu" if op == q4rdna.OP_SWIGLU else "mul_mat",
+            "split": split, "selector": True, "us": round(us, 3), "algo_bytes": algo,
+            "gbs": round(algo / (us * 1e-6) / 1e9, 1), "frac": round(algo / (us * 1e-6) / 1e9 / peak, 4),
+            "host_us_per_call_python": round(host_us, 2)}
+
+
 QKV = (".attn_q.", ".attn_k.", ".attn_v.")
 
 
@@ -311,6 +528,89 @@ def build_step(model: str, rank: int, world: int, device, seed: int, layers: int
         nweights += s.rows * s.K
         abytes += tb + 4 * B * (s.K + s.rows)
     return descs, x_all, y_all, wbytes, abytes, len(names), lay, nweights
+
+
+def step_bytes(model: str, B: int, layers: int = 0, hybrid: bool = False):
+    """(tensors, weight bytes, algorithmic bytes, weights) of one whole decode
+    step (all ranks together), from the model's shapes alone."""
+    from q4rdna import synth
+
+    names = synth.model_tensors(model)
+    if layers:
+        names = [t for t in names if int(t[0].split(".")[1]) < layers]
+    wb = ab = nw = 0
+    for name, N, K in names:
+        tb = synth.q4k_bytes(N, K) if hybrid and any(q in name for q in QKV) else N * K * 34 // 64
+        wb += tb
+        ab += tb + 4 * B * (K + N)
+        nw += N * K
+    return len(names), wb, ab, nw
+
+
+def step_config(args, world: int, p2p: bool):
+    """The `config` object of the step's JSON line, shared by both arms."""
+    ntensors, wbytes, abytes, nweights = step_bytes(args.model, args.batch, args.layers, args.hybrid)
+    return {"workload": f"{args.model} decode-step weight stream: {ntensors} GEMVs batch {args.batch}"
+                        + (f" (first {args.layers} layers only)" if args.layers else "")
+                        + (", qkv-fallback hybrid: attn_q/k/v in Q4_K, the rest in Q4_RDNA" if args.hybrid else "")
+                        + (f", rows sharded over {world} GPUs + " + ("all-gather fused into the plan kernel (P2P stores)"
+                           if p2p else "NCCL all-gather") if world > 1 else ""),
+            "tensors": ntensors, "batch": args.batch, "fused_rmsnorm": bool(args.norm),
+            "flops_per_step": 2 * args.batch * nweights, "weight_bytes_per_step": wbytes,
+            "algo_bytes_per_step": abytes, "parallelism": f"tp{world}" if world > 1 else "none",
+            "l2": f"no flush: {wbytes / 1e9:.2f} GB streamed per step >> 126 MB L2"}
+
+
+def time_drop_in_step(descs, B: int, steps: int, abytes: int, overlap: bool = False):
+    """The step as len(descs) single q4rdna_gemv calls (one launch each, the
+    selector's split per shape, one shared workspace), captured once in a CUDA
+    graph and replayed `steps` times between CUDA events.  overlap: each call
+    with Q4RDNA_CFG_OVERLAP_PREVIOUS (programmatic dependent launch)."""
+    import ctypes
+
+    import torch
+
+    import q4rdna
+
+    L = q4rdna.lib
+    need = max(L.q4rdna_workspace_bytes(d["y"].shape[-1], d["x"].shape[-1], B, q4rdna.OP_PLAIN, None) for d in descs)
+    ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=descs[0]["x"].device)
+    cap = torch.cuda.Stream()
+    cfg = q4rdna.Cfg()
+    cfg.flags = q4rdna.CFG_OVERLAP_PREVIOUS if overlap else 0
+
+    def step():
+        h = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        for d in descs:
+            N, K = d["y"].shape[-1], d["x"].shape[-1]
+            rc = L.q4rdna_gemv(d["tiles"].data_ptr(), d["x"].data_ptr(), d["y"].data_ptr(), N, K, B,
+                               ctypes.byref(cfg), ws.data_ptr(), need, h)
+            if rc != 0:
+                raise RuntimeError(f"q4rdna_gemv {N}x{K}: status {rc}")
+
+    with torch.cuda.stream(cap):
+        step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=cap):
+        step()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        g.replay()
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / steps
+    peak, _ = hbm_peak()
+    gbs = abytes / (us * 1e-6) / 1e9
+    del g
+    return {"how": f"{len(descs)} q4rdna_gemv calls per step (one launch each, selector split), one CUDA graph"
+                   + (", programmatic dependent launch" if overlap else ""),
+            "launches_per_step": len(descs), "us_per_step": round(us, 2), "gbs": round(gbs, 1),
+            "frac": round(gbs / peak, 4)}
 
 
 def run_ours(args):
@@ -406,6 +706,15 @@ def run_ours(args):
                    "achieved": round(kbytes / (k_ms * 1e-3) / 1e9, 1), "frac": round(kbytes / (k_ms * 1e-3) / 1e9 / kpk, 4),
                    "traffic": ncu_traffic(f"q4k_{args.model}_b{B}")}
 
+    # the same step as llama.cpp drives the reference: one drop-in q4rdna_gemv
+    # call per tensor (the selector's split, one shared workspace), captured
+    # once in a CUDA graph and replayed
+    drop_in = None
+    if world == 1 and not args.hybrid and not args.norm:
+        drop_in = time_drop_in_step(descs, B, args.steps, abytes)
+        if B <= 2:
+            drop_in["overlapped"] = time_drop_in_step(descs, B, args.steps, abytes, overlap=True)
+
     # end-to-end: pinned host activations in, outputs out, every step
     x_host = torch.empty(x_all.numel(), dtype=torch.float32, pin_memory=True)
     x_host.copy_(x_all)
@@ -454,16 +763,8 @@ def run_ours(args):
             "data": "synthetic: uniform int4 codes, fp16 scales |N(0,1)|*0.003, x ~ N(0,1) f32 (no Qwen3 weights offline)"
                     + ("; Q4_K tensors: uniform quant and 6-bit scale bytes, d and dmin fp16((0.5+|N(0,1)|)*2e-4)"
                        if args.hybrid else ""),
-            "config": {"workload": f"{args.model} decode-step weight stream: {ntensors} GEMVs batch {B}"
-                                   + (f" (first {args.layers} layers only)" if args.layers else "")
-                                   + (", qkv-fallback hybrid: attn_q/k/v in Q4_K, the rest in Q4_RDNA" if args.hybrid else "")
-                                   + (f", rows sharded over {world} GPUs + " + ("all-gather fused into the plan kernel (P2P stores)"
-                                      if p2p else "NCCL all-gather") if world > 1 else ""),
-                       "tensors": ntensors, "batch": B, "fused_rmsnorm": bool(args.norm), "flops_per_step": 2 * B * nweights * world,
-                       "weight_bytes_per_step": wbytes * world,
-                       "algo_bytes_per_step": total_algo, "parallelism": f"tp{world}" if world > 1 else "none",
-                       "l2": f"no flush: {wbytes * world / 1e9:.2f} GB streamed per step >> 126 MB L2",
-                       "plan_items": info["items"], "plan_grid": info["grid"]},
+            "config": step_config(args, world, p2p),
+            "plan": {"items": info["items"], "grid": info["grid"]},
             "e2e": {"value": round(total_algo / (e2e_ms / args.steps * 1e-3) / 1e9, 2), "unit": UNIT,
                     "us_per_step": round(e2e_ms / args.steps * 1e3, 2),
                     "h2d_bytes_per_step": x_all.numel() * 4, "d2h_bytes_per_step": y_host.numel() * 4},
@@ -474,6 +775,7 @@ def run_ours(args):
                          "traffic": ncu_traffic(f"{args.model}_tp{world}" + (f"_b{B}" if B > 1 else ""))},
             "cpu_baseline": cpu,
             "gpu_launches": launches,
+            **({"drop_in_step": drop_in} if drop_in else {}),
             **({"q4k": q4k_leg} if q4k_leg else {}),
             "clocks": clk.summary(),
         }
@@ -489,9 +791,17 @@ def run_ours(args):
 
 
 def run_reference(args):
+    """The reference's own CPU GEMV on the host cores, on this arm's config.
+    reference_q4_rdna (source/q4rdna_gemv_bench.hip:189-211) exists only at
+    12288 x 4096 (ROWS, COLUMNS at :17-18), so each step times a bounded sample
+    of the workload: that shape, which is the step's ffn_gate / ffn_up tensors
+    (72 of the Qwen3-8B step's 252), one call per host thread at a time for
+    --ref-step-seconds.  The rate is algorithmic GB/s like our arm's; the
+    step-equivalent time is the whole step's bytes at that rate."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     steps = []
     thr = cpu_count()
     for i in range(args.warmup + args.steps):
@@ -499,11 +809,18 @@ def run_reference(args):
         if i >= args.warmup:
             steps.append(v)
     v = statistics.mean(steps)
+    cfg = step_config(args, world, world > 1 and args.gather == "p2p" and not args.hybrid)
+    step_us = cfg["algo_bytes_per_step"] / (v * 1e9) * 1e6
     return {
         "metric": METRIC, "impl": "reference", "value": round(v, 3), "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f32 (reference CPU GEMV)", "data": "synthetic, same distributions",
-        "config": {"workload": f"{args.model} decode-step weight stream (reference CPU GEMV on host cores)"},
+        "vs_baseline": None, "dtype": "f32 (reference CPU GEMV)",
+        "data": "synthetic: uniform int4 codes, fp16 scales |N(0,1)|*0.003, x ~ N(0,1) f32 (no Qwen3 weights offline)",
+        "config": cfg,
+        "us_per_step": round(step_us, 1),
+        "sample": ("each step: " + sample + "; reference_q4_rdna is fixed at 12288x4096 "
+                   "(q4rdna_gemv_bench.hip:17-18), the shape of the step's ffn_gate/ffn_up tensors; "
+                   "us_per_step = the whole step's algorithmic bytes at the measured rate"),
         "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": thr, "kind": kind, "sample": sample},
         "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -534,6 +851,14 @@ def main():
                     help="activation columns per GEMV (1..16; 3..16 run the tile path)")
     ap.add_argument("--hybrid", action="store_true",
                     help="the reference's qkv-fallback scope: attn_q/k/v as Q4_K tensors, the rest Q4_RDNA")
+    ap.add_argument("--single", action="store_true",
+                    help="us per GEMV through the drop-in entry points (configs 0 and 1) instead of the step")
+    ap.add_argument("--single-sweep", action="store_true", help="--single: also force split 1..16")
+    ap.add_argument("--single-shapes", default="", help="--single: comma-separated subset of the shapes")
+    ap.add_argument("--single-launches", type=int, default=1000, help="--single: calls per timed graph")
+    ap.add_argument("--single-no-hook", action="store_true", help="--single: skip the name-keyed hook leg")
+    ap.add_argument("--single-ncu", action="store_true",
+                    help="--single: only 3 eager calls per shape at the selector's split (for an ncu launch list)")
     ap.add_argument("--layers", type=int, default=0,
                     help="only the first L layers (small cases for profiling); 0 = the whole model")
     args = ap.parse_args()
@@ -546,6 +871,8 @@ def main():
     os.dup2(2, 1)
     if args.pack:
         out = run_pack(args)
+    elif args.single:
+        out = run_single(args)
     else:
         out = run_reference(args) if args.impl == "reference" else run_ours(args)
     if out is not None:

@@ -58,11 +58,20 @@ typedef enum q4rdna_op {
 } q4rdna_op;
 
 /* Launch options.  split = 0 lets the selector choose the split-K factor;
- * split > 0 forces it (clamped to [1, K/64]). */
+ * split > 0 forces it (clamped to [1, K/64]).  flags: Q4RDNA_CFG_* bits. */
 typedef struct q4rdna_cfg {
     int split;
-    int reserved[7];
+    int flags;
+    int reserved[6];
 } q4rdna_cfg;
+
+/* Single calls at B = 1..2 without a norm: let the GEMV start streaming its
+ * first weights while the previous kernel on the stream finishes (programmatic
+ * dependent launch).  Everything the previous kernels write (x, y, add, the
+ * workspace) is touched only after they complete; only the weight tiles are
+ * read early, so the caller guarantees that no kernel still running on the
+ * stream writes them (true for weights loaded once, e.g. a sidecar). */
+#define Q4RDNA_CFG_OVERLAP_PREVIOUS 1
 
 const char *q4rdna_status_string(q4rdna_status s);
 /* Library version string. */
@@ -105,9 +114,7 @@ q4rdna_status q4rdna_gemv_swiglu(const uint8_t *up_tiles, const uint8_t *gate_ti
  * sum of h^2 is taken while the activation groups are prepared, and the scale
  * is applied once per output (after the split-K reduction when S > 1, splits
  * in ascending order).  op, gate_tiles and add as in q4rdna_gemv_swiglu /
- * q4rdna_gemv_add; the workspace is sized by q4rdna_workspace_bytes.  Runs on
- * the default kernels only (Q4RDNA_ERR_UNSUPPORTED under Q4RDNA_KERNEL=ldg or
- * i8tma at B <= 2). */
+ * q4rdna_gemv_add; the workspace is sized by q4rdna_workspace_bytes. */
 q4rdna_status q4rdna_gemv_rmsnorm(const uint8_t *tiles, const uint8_t *gate_tiles, const float *h,
                                   const float *norm_weight, float eps, const float *add, float *y, int N, int K,
                                   int B, int op, const q4rdna_cfg *cfg, void *workspace, size_t workspace_bytes,
@@ -267,6 +274,13 @@ q4rdna_status q4rdna_plan_set_segments(q4rdna_plan *plan, int segments);
 q4rdna_status q4rdna_plan_set_gather(q4rdna_plan *plan, int world, int rank, const float *y_base,
                                      size_t rank_floats, float *const *gathered0, float *const *gathered1,
                                      uint32_t *const *flags);
+/* Bound of the fused gather's flag wait: a run stops waiting for the peers'
+ * flags after about `microseconds` (0: the default, about 2 s), sets bit 1 of
+ * q4rdna_take_fault and returns, so a rank that never arrives shows up on the
+ * host as a fault flag instead of a hung stream.  The wait is a polling loop
+ * with ~0.5 us sleeps, so the bound is approximate.  May be called before or
+ * after q4rdna_plan_set_gather.  No reference counterpart. */
+q4rdna_status q4rdna_plan_set_gather_timeout(q4rdna_plan *plan, uint32_t microseconds);
 /* Gathered buffer (0 or 1) that the plan's last run filled; -1 before the first
  * run or without a gather. */
 int q4rdna_plan_gather_parity(const q4rdna_plan *plan);
@@ -329,17 +343,19 @@ int q4rdna_mul_mat_glu(const char *up_name, int64_t up_ne0, int64_t up_ne1, cons
 uint64_t q4rdna_launch_count(void);
 uint64_t q4rdna_registry_hits(const char *weight_name);
 /* Device-side fault flags of the GEMV kernels since the last call, then cleared
- * (synchronises the device).  Bit 0: a pipeline wait ran past its iteration
- * limit (about 2 s), so the kernel stopped early and its outputs are invalid.
- * Bit 1: a fused gather (q4rdna_plan_set_gather) stopped waiting for a peer's
- * flag (about 2 s), so the gathered buffer of that run is incomplete.
- * 0 = no fault; 0xffffffff = the flag could not be read.  No reference
- * counterpart (the reference kernels never wait). */
+ * (synchronises the device).  Bit 1: a fused gather (q4rdna_plan_set_gather)
+ * stopped waiting for a peer's flag (q4rdna_plan_set_gather_timeout), so the
+ * gathered buffer of that run is incomplete; the GEMV outputs of this rank
+ * (y) are complete.  Bit 0 is no longer set by any kernel.  0 = no fault;
+ * 0xffffffff = the flag could not be read.  No reference counterpart (the
+ * reference kernels never wait). */
 uint32_t q4rdna_take_fault(void);
 /* Prints the reference's exit-time summary to stderr (also run at exit once the
  * registry has loaded); LLAMA_Q4_RDNA_TRACE adds per-tensor hit lines. */
 void q4rdna_report_stats(void);
-/* Drops the process-wide registry (frees its device memory).  For tests. */
+/* Drops the process-wide registry (frees its device memory and workspaces)
+ * and the no-alloc entry point's cached scratch addresses.  For tests, and
+ * after a cudaDeviceReset. */
 void q4rdna_registry_reset(void);
 
 #if defined(__GNUC__)

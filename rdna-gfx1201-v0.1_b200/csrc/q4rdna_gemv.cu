@@ -1,39 +1,27 @@
-// Q4_RDNA group-64 GEMV for B200 (sm_100a).
+// Q4_RDNA group-64 GEMV for B200 (sm_100a): shared device helpers, the plan /
+// single-call host side, and the fused tensor-parallel gather.
 //
-// One warp work item = one 128-row block (four 32-row tiles) x one K-range of
-// `Gs` groups, for one tensor (two for the fused SwiGLU).  The warp streams its
-// tiles straight from HBM with 128-bit loads, unpacks the int4 codes to fp16 in
-// registers and lets the tensor cores (mma.sync m16n8k16, f32 accumulate) do
-// the dot products against the activation, which is carried as an exact
-// fp16 hi + lo pair per element.  The fp16 group scale is applied once per
-// (row, group) in f32, as the reference does (source/q4rdna.cu:370-371).
-// Split-K partial sums go to a workspace; the last warp to finish a row block
-// (arrival ticket) adds them in split order and applies the add / SwiGLU
-// epilogue, so results are deterministic.
+// The kernels live in two headers included below:
+//   q4rdna_gemv_i8.cuh  B = 1..2: one warp work item = one 128-row block (four
+//                       32-row tiles) x one K-range of Gs groups, streamed with
+//                       128-bit loads into a register pipeline; int8 tensor-core
+//                       MMAs (mma.sync m16n8k32) sum each group exactly;
+//   q4rdna_gemv_cta.cuh single calls at B = 1..2: one CTA item = 128 rows x a
+//                       K-range split again over the CTA's 8 warps, so a lone
+//                       GEMV keeps the whole GPU streaming;
+//   q4rdna_gemv_mb.cuh  B = 3..16: the tile path, one CTA work item of 128 rows,
+//                       the full m16n8k32 fragment over the batch columns.
+// Both scale each 64-element activation group by a power of two, round it to
+// an integer X (|X| <= 2^30) and feed its four balanced base-256 digits to the
+// int8 MMAs; the fp16 group scale is applied once per (row, group) in f32, as
+// the reference does (source/q4rdna.cu:370-371).  Split-K partial sums go to a
+// workspace; the last warp (or CTA) to finish a row block (arrival ticket) adds
+// them in split order and applies the add / SwiGLU epilogue, so results are
+// deterministic.
 //
-// Why tensor cores at batch 1: at 6.5 TB/s the stream is ~12e12 weights/s,
-// which leaves ~3 issue slots per weight on the CUDA cores.  Unpack + convert +
-// FFMA per weight does not fit; here the per-weight cost is ~1.1 integer/half
-// instructions plus 1/8 of an MMA issue.
-//
-// Register-fragment mapping (m16n8k16, A row-major, B col-major):
-//   lane L: grp = L>>2 (0..7), c = L&3; tile t = grp>>1, half h = grp&1.
-//   For MMA step m (0..7) the lane's 16-byte load is tile t, code bytes
-//   64 + 128m + 32c + 16h: rows 16h..16h+15 of column pair i = 4m + c.
-//   Its j-th 32-bit word (j = 0..3) holds rows rho = 16h + 4j + {0,1,2,3} and
-//   feeds MMA j.  Nibbles are expanded with the fp16 magic-number trick:
-//     P0 = (b0.lo, b2.lo), P1 = (b0.hi, b2.hi), P2 = (b1.lo, b3.lo), P3 = (b1.hi, b3.hi)
-//   and used as A registers a0a1 = P0, a2a3 = P2, a4a5 = P1, a6a7 = P3.  So MMA
-//   row grp carries weight rows rho+0 (even k-slots) and rho+2 (odd k-slots),
-//   MMA row grp+8 carries rho+1 / rho+3.  The B operand separates the two
-//   slots into different columns: column n = 4*bb + role, role 0/1 = slot 0
-//   (x_hi / x_lo), role 2/3 = slot 1 (x_hi / x_lo), bb = batch within the
-//   MMA's batch pair.  D column pairs (2c, 2c+1) therefore hold hi and lo for
-//   rows rho + 2(c&1) (+1 for the grp+8 half) of batch 2*nb + (c>>1).
-// Accumulation order of an output: inside a group the tensor core sums exact
-// products (int4 x fp16) in f32; groups of one split are added in ascending
-// order, each as sum = fma(scale * 2^e, hi + lo, sum); splits are then added
-// in ascending split order in f32.
+// Accumulation order of an output: exact int32 inside a group; groups of one
+// split in ascending order, sum = fma(scale / 16, v * 2^e, sum) with v the
+// recombined digit sums; splits in ascending split order in f32.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -101,161 +89,12 @@ __device__ __forceinline__ uint32_t ld_stream4(const uint8_t *p) {
     return v;
 }
 
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                         uint32_t a3, uint32_t b0, uint32_t b1) {
-    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-        "{%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-// (1024 + (n ^ 8)) - 1032 = signed code, exact in fp16.
-__device__ __forceinline__ uint32_t unbias_lo(uint32_t p) {
-    uint32_t r;
-    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(p), "r"(0x64086408u));
-    return r;
-}
-// (1024 + 16 (n ^ 8)) / 16 - 72 = signed code, exact in fp16.
-__device__ __forceinline__ uint32_t unbias_hi(uint32_t p) {
-    uint32_t r;
-    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(p), "r"(0x2C002C00u), "r"(0xD480D480u));
-    return r;
-}
-
-// One 32-bit code word (4 rows x 1 column pair) -> the four A registers.
-__device__ __forceinline__ void word_to_a(uint32_t w, uint32_t &a0, uint32_t &a1, uint32_t &a2,
-                                          uint32_t &a3) {
-    const uint32_t w8 = w >> 8;
-    a0 = unbias_lo((w & 0x000F000Fu) ^ 0x64086408u);   // (b0.lo, b2.lo)
-    a1 = unbias_lo((w8 & 0x000F000Fu) ^ 0x64086408u);  // (b1.lo, b3.lo)
-    a2 = unbias_hi((w & 0x00F000F0u) ^ 0x64806480u);   // (b0.hi, b2.hi)
-    a3 = unbias_hi((w8 & 0x00F000F0u) ^ 0x64806480u);  // (b1.hi, b3.hi)
-}
-
 __device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
-}
-
-// Per-warp shared scratch: one group of the activation as (x_hi | x_lo << 16)
-// per element for each batch column of the pass, and the power of two that
-// undoes the group's normalisation.
-template <int NB>
-struct __align__(16) WarpSmem {
-    uint32_t xq[2 * NB][Q4_GROUP];
-    float up[2 * NB];
-};
-
-// Normalise one 64-element group of x by a power of two so that its largest
-// magnitude lands in [2^14, 2^15) (exact), then split every element into
-// x_hi = fp16(x) and x_lo = fp16(x - x_hi); x_hi + x_lo keeps ~22 significant
-// bits and the fp16 range can no longer overflow or underflow the group.
-__device__ __forceinline__ void prep_group(float2 v, uint32_t *xq_row, float *up, int lane) {
-    const float m = warp_max(fmaxf(fabsf(v.x), fabsf(v.y)));
-    float f = 1.0f, u = 1.0f;
-    if (m > 0.0f) {
-        const uint32_t e = max((__float_as_uint(m) >> 23) & 0xffu, 15u);
-        f = __uint_as_float((268u - e) << 23);  // 2^(141 - e)
-        u = __uint_as_float((e - 14u) << 23);   // 2^(e - 141)
-    }
-    const float s0 = v.x * f, s1 = v.y * f;
-    const __half2 hi = __floats2half2_rn(s0, s1);
-    const float2 hf = __half22float2(hi);
-    const __half2 lo = __floats2half2_rn(s0 - hf.x, s1 - hf.y);
-    const uint32_t hb = *reinterpret_cast<const uint32_t *>(&hi);
-    const uint32_t lb = *reinterpret_cast<const uint32_t *>(&lo);
-    uint2 q;
-    q.x = __byte_perm(hb, lb, 0x5410);  // element 2*lane:   hi | lo << 16
-    q.y = __byte_perm(hb, lb, 0x7632);  // element 2*lane+1
-    reinterpret_cast<uint2 *>(xq_row)[lane] = q;
-    if (lane == 0) *up = u;
-}
-
-// Code words and scale words of one (tensor, group) step for this lane.
-struct StepBuf {
-    uint4 q[8];     // MMA step m: 16 code bytes
-    uint32_t s[4];  // fp16 scale pair of the lane's two rows for MMA j
-};
-
-__device__ __forceinline__ void load_step(StepBuf &b, const uint8_t *tile, bool valid, int c, int h) {
-    if (valid) {
-        const uint8_t *qp = tile + Q4_SCALE_BYTES + 32 * c + 16 * h;
-#pragma unroll
-        for (int m = 0; m < 8; ++m) b.q[m] = ld_stream16(qp + 128 * m);
-        const uint8_t *sp = tile + 32 * h + 4 * (c & 1);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) b.s[j] = ld_stream4(sp + 8 * j);
-    } else {
-#pragma unroll
-        for (int m = 0; m < 8; ++m) b.q[m] = make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) b.s[j] = 0u;
-    }
-}
-
-__device__ __forceinline__ uint32_t word_of(const uint4 &v, int j) {
-    return j == 0 ? v.x : (j == 1 ? v.y : (j == 2 ? v.z : v.w));
-}
-
-// One group of one tensor: 32 MMAs per warp (4 row slices x 8 k-steps x NB
-// batch pairs), then the per-(row, group) scale in f32.  While slot m of `buf`
-// is consumed it is refilled with slot m of the next step (`next`, when
-// non-null), so one step of loads stays in flight with one buffer of registers.
-template <int NB>
-__device__ __forceinline__ void compute_step(StepBuf &buf, const uint8_t *next, bool valid, int c, int h,
-                                             const WarpSmem<NB> &sm, float (&acc)[4][NB][2], int lane,
-                                             const uint32_t (&sel)[NB], const int (&xrow)[NB],
-                                             const int (&urow)[NB]) {
-    float D[4][NB][4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-        for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-            for (int r = 0; r < 4; ++r) D[j][nb][r] = 0.0f;
-    uint32_t sw[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) sw[j] = buf.s[j];
-    const bool refill = next != nullptr && valid;
-    const uint8_t *nq = next + Q4_SCALE_BYTES + 32 * c + 16 * h;
-    if (refill) {
-        const uint8_t *sp = next + 32 * h + 4 * (c & 1);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) buf.s[j] = ld_stream4(sp + 8 * j);
-    }
-    const int c4 = lane & 3;
-#pragma unroll
-    for (int m = 0; m < 8; ++m) {
-        const uint4 cur = buf.q[m];
-        if (refill) buf.q[m] = ld_stream16(nq + 128 * m);
-        uint32_t b0[NB], b1[NB];
-#pragma unroll
-        for (int nb = 0; nb < NB; ++nb) {
-            const uint2 p = *reinterpret_cast<const uint2 *>(&sm.xq[xrow[nb]][8 * m + 2 * c4]);
-            b0[nb] = __byte_perm(p.x, 0u, sel[nb]);
-            b1[nb] = __byte_perm(p.y, 0u, sel[nb]);
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            uint32_t a0, a1, a2, a3;
-            word_to_a(word_of(cur, j), a0, a1, a2, a3);
-#pragma unroll
-            for (int nb = 0; nb < NB; ++nb) mma16816(D[j][nb], a0, a1, a2, a3, b0[nb], b1[nb]);
-        }
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const float2 sc = __half22float2(*reinterpret_cast<const __half2 *>(&sw[j]));
-#pragma unroll
-        for (int nb = 0; nb < NB; ++nb) {
-            const float u = sm.up[urow[nb]];
-            acc[j][nb][0] = fmaf(sc.x * u, D[j][nb][0] + D[j][nb][1], acc[j][nb][0]);
-            acc[j][nb][1] = fmaf(sc.y * u, D[j][nb][2] + D[j][nb][3], acc[j][nb][1]);
-        }
-    }
 }
 
 // Final store of one output: y, and its copies in the ranks' gathered buffers
@@ -318,133 +157,6 @@ __device__ __forceinline__ void reduce_splits(const Task &T, int rb, int B, int 
     if (lane == 0) atomicExch(&T.ticket[rb], 0u);
 }
 
-// Epilogue of one work item: store (S == 1), or write the split partials and,
-// in the last warp to arrive at the row block, add the splits in ascending
-// order and apply the add / SwiGLU epilogue.
-template <int NB, bool DUAL>
-__device__ __forceinline__ void finish_item(const Task &T, int rb, int s, int B,
-                                            float (&acc)[DUAL ? 2 : 1][4][NB][2], int lane, bool valid,
-                                            int tile_row, int h, int c) {
-    // Rows of this lane: tile t, rows 16h + 4j + 2(c&1) + e; batch 2nb + (c>>1).
-    const int row0 = tile_row * Q4_TILE_ROWS + 16 * h + 2 * (c & 1);
-    if (T.S == 1) {
-        if (valid) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-#pragma unroll
-                for (int nb = 0; nb < NB; ++nb) {
-                    const int b = 2 * nb + (c >> 1);
-                    if (b >= B) continue;
-#pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        const size_t idx = (size_t)b * T.N + row0 + 4 * j + e;
-                        put_y(T, idx, finish(acc[0][j][nb][e], acc[DUAL ? 1 : 0][j][nb][e], T.op, T.add, idx));
-                    }
-                }
-        }
-        return;
-    }
-
-    constexpr int planes = DUAL ? 2 : 1;
-    if (valid) {
-#pragma unroll
-        for (int q = 0; q < planes; ++q)
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-#pragma unroll
-                for (int nb = 0; nb < NB; ++nb) {
-                    const int b = 2 * nb + (c >> 1);
-                    if (b >= B) continue;
-#pragma unroll
-                    for (int e = 0; e < 2; ++e)
-                        __stcg(&T.part[(((size_t)s * planes + q) * B + b) * T.N + row0 + 4 * j + e], acc[q][j][nb][e]);
-                }
-    }
-    __threadfence();
-    __syncwarp();
-    unsigned prev = 0;
-    if (lane == 0) prev = atomicAdd(&T.ticket[rb], 1u);
-    prev = __shfl_sync(0xffffffffu, prev, 0);
-    if (prev != (unsigned)(T.S - 1)) return;
-
-    reduce_splits<DUAL>(T, rb, B, lane);
-}
-
-// One work item: row block rb, split s of task T; NB batch pairs (B <= 2*NB).
-template <int NB, bool DUAL>
-__device__ __forceinline__ void run_item(const Task &T, long long local, int B, WarpSmem<NB> &sm, int lane) {
-    const int rb = (int)(local / T.S), s = (int)(local % T.S);
-    const int g0 = s * T.Gs, ng = min(T.Gs, T.G - g0);
-    const int grp = lane >> 2, c = lane & 3, t = grp >> 1, h = grp & 1;
-    const int tile_row = rb * Q4_BLOCK_TILES + t;
-    const bool valid = tile_row < (T.N >> 5);
-    const size_t tile0 = ((size_t)tile_row * T.G + g0) * Q4_TILE_BYTES;
-    const uint8_t *base0 = T.w + (valid ? tile0 : 0);
-    const uint8_t *base1 = DUAL ? T.w2 + (valid ? tile0 : 0) : nullptr;
-
-    // B operand selectors: lane's column is n = lane>>2 -> batch 2nb + (lane>>4), role (lane>>2)&3.
-    uint32_t sel[NB];
-    int xrow[NB], urow[NB];
-    {
-        const int role = (lane >> 2) & 3;
-        const uint32_t role_sel = role == 0 ? 0x4410u : role == 1 ? 0x4432u : role == 2 ? 0x1044u : 0x3244u;
-#pragma unroll
-        for (int nb = 0; nb < NB; ++nb) {
-            const int bx = 2 * nb + (lane >> 4);
-            sel[nb] = bx < B ? role_sel : 0x4444u;
-            xrow[nb] = min(bx, B - 1);
-            urow[nb] = min(2 * nb + (c >> 1), B - 1);
-        }
-    }
-
-    float acc[DUAL ? 2 : 1][4][NB][2];
-#pragma unroll
-    for (int q = 0; q < (DUAL ? 2 : 1); ++q)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-#pragma unroll
-            for (int nb = 0; nb < NB; ++nb) acc[q][j][nb][0] = acc[q][j][nb][1] = 0.0f;
-
-    // Activation of the first group; later groups are fetched one group ahead.
-    float2 xv[2 * NB];
-#pragma unroll
-    for (int b = 0; b < 2 * NB; ++b)
-        xv[b] = b < B ? __ldg(reinterpret_cast<const float2 *>(T.x + (size_t)b * T.K + (size_t)g0 * Q4_GROUP) + lane)
-                      : make_float2(0.0f, 0.0f);
-
-    const int nsteps = ng * (DUAL ? 2 : 1);
-    auto step_tile = [&](int st) -> const uint8_t * {
-        const int tt = DUAL ? (st & 1) : 0, gl = DUAL ? (st >> 1) : st;
-        return (tt ? base1 : base0) + (size_t)gl * Q4_TILE_BYTES;
-    };
-    StepBuf buf;
-    load_step(buf, step_tile(0), valid, c, h);
-    for (int st = 0; st < nsteps; ++st) {
-        const int tt = DUAL ? (st & 1) : 0, gl = DUAL ? (st >> 1) : st;
-        if (tt == 0) {
-            __syncwarp();
-#pragma unroll
-            for (int b = 0; b < 2 * NB; ++b)
-                if (b < B) prep_group(xv[b], sm.xq[b], &sm.up[b], lane);
-            if (gl + 1 < ng) {
-#pragma unroll
-                for (int b = 0; b < 2 * NB; ++b)
-                    if (b < B)
-                        xv[b] = __ldg(reinterpret_cast<const float2 *>(T.x + (size_t)b * T.K +
-                                                                       (size_t)(g0 + gl + 1) * Q4_GROUP) + lane);
-            }
-            __syncwarp();
-        }
-        const uint8_t *next = st + 1 < nsteps ? step_tile(st + 1) : nullptr;
-        if (DUAL && tt == 1)
-            compute_step<NB>(buf, next, valid, c, h, sm, acc[DUAL ? 1 : 0], lane, sel, xrow, urow);
-        else
-            compute_step<NB>(buf, next, valid, c, h, sm, acc[0], lane, sel, xrow, urow);
-    }
-
-    finish_item<NB, DUAL>(T, rb, s, B, acc, lane, valid, tile_row, h, c);
-}
-
 __device__ __forceinline__ const Task &find_task(const Launch &L, long long item) {
     if (L.table == nullptr) return L.one;
     int lo = 0, hi = L.ntasks - 1;
@@ -453,21 +165,6 @@ __device__ __forceinline__ const Task &find_task(const Launch &L, long long item
         if (L.table[mid].item_begin <= item) lo = mid; else hi = mid - 1;
     }
     return L.table[lo];
-}
-
-// Persistent over work items: warp w of the grid takes items w, w + nwarps, ...
-template <int NB>
-__global__ void __launch_bounds__(kThreads, NB == 1 ? 2 : 1) q4_gemv_kernel(const __grid_constant__ Launch L) {
-    __shared__ WarpSmem<NB> smem[kWarps];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long nw = (long long)gridDim.x * kWarps;
-    for (long long it = (long long)blockIdx.x * kWarps + warp; it < L.total_items; it += nw) {
-        const Task &T = find_task(L, it);
-        if (T.op == Q4RDNA_OP_SWIGLU)
-            run_item<NB, true>(T, it - T.item_begin, L.B, smem[warp], lane);
-        else
-            run_item<NB, false>(T, it - T.item_begin, L.B, smem[warp], lane);
-    }
 }
 
 // Debug dequantisation: one thread per (row, group) writes 64 exact values.
@@ -487,125 +184,64 @@ __global__ void q4_dequant_kernel(const uint8_t *tiles, float *W, int N, int K) 
     }
 }
 
-#include "q4rdna_gemv_tma.cuh"
+// Device-side fault flags, read and cleared by q4rdna_take_fault (bit 1: a fused
+// gather stopped waiting for a peer's flag).
+__device__ unsigned int g_fault;
+
 #include "q4rdna_gemv_i8.cuh"
-#include "q4rdna_gemv_i8_tma.cuh"
+#include "q4rdna_gemv_cta.cuh"
 #include "q4rdna_gemv_mb.cuh"
-#include "q4rdna_gemv_mbh.cuh"
 
 // ------------------------------------------------------------------ host side
 
 constexpr int kMaxDevices = 64;
-constexpr int kMaxPassBatch = 4;  // batch columns the batch-1 kernels can take (BB <= 4)
+constexpr int kTileMinBatch = 3;  // B >= 3 runs on the tile path (q4rdna_gemv_mb.cuh)
 std::atomic<uint64_t> g_launches{0};
-
-// Kernel variants: the int8 tensor-core kernel with register loads (default,
-// fastest measured), the same math fed by a TMA ring, or the fp16 tensor-core
-// kernel.  Q4RDNA_KERNEL=i8|i8tma|ldg selects one for A/B measurements.
-enum Variant { kI8 = 0, kI8Tma, kLdg, kVariants };
-constexpr int kDefaultVariant = kI8;
-
-int variant() {
-    static const int v = [] {
-        const char *e = std::getenv("Q4RDNA_KERNEL");
-        if (e == nullptr || *e == '\0') return kDefaultVariant;
-        const char *names[kVariants] = {"i8", "i8tma", "ldg"};
-        for (int i = 0; i < kVariants; ++i)
-            if (std::strcmp(e, names[i]) == 0) return i;
-        return kDefaultVariant;
-    }();
-    return v;
-}
 
 struct KernelCfg {
     const void *fn;
-    int threads, smem, warps;
+    int threads, warps;  // warps: work items in flight per CTA (1 on the tile path)
 };
 
-// Batch class of a launch: 0 -> 1 column, 1 -> 2, 2 -> 3..4, 3 -> 5..8, 4 -> 9..16.
-constexpr int kBatchClasses = 5;
-int batch_class(int pb) { return pb <= 1 ? 0 : pb == 2 ? 1 : pb <= 4 ? 2 : pb <= 8 ? 3 : 4; }
-int class_batch(int bc) { return bc == 0 ? 1 : bc == 1 ? 2 : bc == 2 ? 4 : bc == 3 ? 8 : 16; }
-
-// Tile path for B >= tile_min_batch(): one work item per CTA.  The int8
-// kernel (q4rdna_gemv_mb.cuh) by default; Q4RDNA_TILE=f16 selects the f16 one
-// (q4rdna_gemv_mbh.cuh), kept for A/B measurements: on the Qwen3-8B step it
-// took 1695 / 1729 / 3441 us at B = 4 / 8 / 16 against 1249 / 1281 / 2373 us
-// for the int8 kernel (long-scoreboard bound at 142 registers, 3 CTAs/SM).
-bool tile_i8() {
-    static const bool v = [] {
-        const char *e = std::getenv("Q4RDNA_TILE");
-        return e == nullptr || std::strcmp(e, "f16") != 0;
-    }();
-    return v;
-}
+// Batch class of a launch: 0 -> 1 column, 1 -> 2, 2 -> 3..8, 3 -> 9..16.
+constexpr int kBatchClasses = 4;
+int batch_class(int pb) { return pb <= 1 ? 0 : pb == 2 ? 1 : pb <= 8 ? 2 : 3; }
+int class_batch(int bc) { return bc == 0 ? 1 : bc == 1 ? 2 : bc == 2 ? 8 : 16; }
 
 template <bool NORM>
 KernelCfg mb_cfg_n(int pb, bool dual) {
-    if (tile_i8()) {
-        if (pb <= 8)
-            return dual ? KernelCfg{(const void *)q4_gemv_mb_kernel<8, true, NORM>, kMbThreads, 0, 1}
-                        : KernelCfg{(const void *)q4_gemv_mb_kernel<8, false, NORM>, kMbThreads, 0, 1};
-        return dual ? KernelCfg{(const void *)q4_gemv_mb_kernel<16, true, NORM>, kMbThreads, 0, 1}
-                    : KernelCfg{(const void *)q4_gemv_mb_kernel<16, false, NORM>, kMbThreads, 0, 1};
-    }
     if (pb <= 8)
-        return dual ? KernelCfg{(const void *)q4_gemv_mbh_kernel<8, true, NORM>, kMbThreads, 0, 1}
-                    : KernelCfg{(const void *)q4_gemv_mbh_kernel<8, false, NORM>, kMbThreads, 0, 1};
-    return dual ? KernelCfg{(const void *)q4_gemv_mbh_kernel<16, true, NORM>, kMbThreads, 0, 1}
-                : KernelCfg{(const void *)q4_gemv_mbh_kernel<16, false, NORM>, kMbThreads, 0, 1};
-}
-KernelCfg mb_cfg(int pb, bool dual, bool norm) { return norm ? mb_cfg_n<true>(pb, dual) : mb_cfg_n<false>(pb, dual); }
-
-template <bool DUAL>
-KernelCfg i8_cfg(int pb, bool norm) {
-    if (norm) {
-        if (pb <= 1) return KernelCfg{(const void *)q4_gemv_i8_kernel<1, DUAL, true>, kThreads, 0, kWarps};
-        if (pb == 2) return KernelCfg{(const void *)q4_gemv_i8_kernel<2, DUAL, true>, kThreads, 0, kWarps};
-        return KernelCfg{(const void *)q4_gemv_i8_kernel<4, DUAL, true>, kThreads, 0, kWarps};
-    }
-    if (pb <= 1) return KernelCfg{(const void *)q4_gemv_i8_kernel<1, DUAL, false>, kThreads, 0, kWarps};
-    if (pb == 2) return KernelCfg{(const void *)q4_gemv_i8_kernel<2, DUAL, false>, kThreads, 0, kWarps};
-    return KernelCfg{(const void *)q4_gemv_i8_kernel<4, DUAL, false>, kThreads, 0, kWarps};
+        return dual ? KernelCfg{(const void *)q4_gemv_mb_kernel<8, true, NORM>, kMbThreads, 1}
+                    : KernelCfg{(const void *)q4_gemv_mb_kernel<8, false, NORM>, kMbThreads, 1};
+    return dual ? KernelCfg{(const void *)q4_gemv_mb_kernel<16, true, NORM>, kMbThreads, 1}
+                : KernelCfg{(const void *)q4_gemv_mb_kernel<16, false, NORM>, kMbThreads, 1};
 }
 
-KernelCfg i8tma_cfg(int pb) {
-    using R = I8Ring;
-    if (pb <= 1) return KernelCfg{(const void *)q4_gemv_i8_tma_kernel<1, R>, R::THREADS, R::SMEM_BYTES, R::WARPS};
-    if (pb == 2) return KernelCfg{(const void *)q4_gemv_i8_tma_kernel<2, R>, R::THREADS, R::SMEM_BYTES, R::WARPS};
-    return KernelCfg{(const void *)q4_gemv_i8_tma_kernel<4, R>, R::THREADS, R::SMEM_BYTES, R::WARPS};
+template <bool DUAL, bool NORM>
+KernelCfg i8_cfg_n(int pb) {
+    return pb <= 1 ? KernelCfg{(const void *)q4_gemv_i8_kernel<1, DUAL, NORM>, kThreads, kWarps}
+                   : KernelCfg{(const void *)q4_gemv_i8_kernel<2, DUAL, NORM>, kThreads, kWarps};
 }
 
-// dual: the launch holds a SwiGLU task (kernels without the SwiGLU path need fewer registers).
-// Smallest batch that runs on the tile path.  Default 3: measured on the
-// Qwen3-8B step, the tile path takes B = 3..4 at a third of the batch-1 int8
-// kernel's time and ties it at B = 2.  Q4RDNA_TILE_MIN_BATCH (1, 2, 3 or 5)
-// overrides it for A/B measurements.
-int tile_min_batch() {
-    static const int v = [] {
-        const char *e = std::getenv("Q4RDNA_TILE_MIN_BATCH");
-        const int t = (e != nullptr && *e != '\0') ? std::atoi(e) : 3;
-        return std::max(1, std::min(t, kMaxPassBatch + 1));
-    }();
-    return v;
+// dual: the launch holds a SwiGLU task; norm: it holds a fused-RMSNorm task.
+// Kernels compiled without those paths need fewer registers.  Occupancy and
+// grids are taken from the kernels without a norm (the norm kernels use the
+// same registers +- 5).
+KernelCfg kernel_cfg(int pb, bool dual = true, bool norm = false) {
+    if (pb >= kTileMinBatch) return norm ? mb_cfg_n<true>(pb, dual) : mb_cfg_n<false>(pb, dual);
+    if (norm) return dual ? i8_cfg_n<true, true>(pb) : i8_cfg_n<false, true>(pb);
+    return dual ? i8_cfg_n<true, false>(pb) : i8_cfg_n<false, false>(pb);
 }
 
-// norm: the launch holds a fused-RMSNorm task (occupancy and grids are taken
-// from the kernels without it; the norm kernels use the same registers +- 5).
-KernelCfg kernel_cfg(int v, int pb, bool dual = true, bool norm = false) {
-    if (pb >= tile_min_batch()) return mb_cfg(pb, dual, norm);
-    switch (v) {
-        case kI8Tma: return i8tma_cfg(pb);
-        case kLdg:
-            return pb <= 2 ? KernelCfg{(const void *)q4_gemv_kernel<1>, kThreads, 0, kWarps}
-                           : KernelCfg{(const void *)q4_gemv_kernel<2>, kThreads, 0, kWarps};
-        default: return dual ? i8_cfg<true>(pb, norm) : i8_cfg<false>(pb, norm);
-    }
+const void *cta_kernel(int pb, bool dual) {
+    if (pb <= 1) return dual ? (const void *)q4_gemv_cta_kernel<1, true> : (const void *)q4_gemv_cta_kernel<1, false>;
+    return dual ? (const void *)q4_gemv_cta_kernel<2, true> : (const void *)q4_gemv_cta_kernel<2, false>;
 }
 
 struct DeviceInfo {
     int sms = 0;
-    int occ[kVariants][kBatchClasses][2] = {};  // resident CTAs per SM: variant, batch class, SwiGLU (0: unknown)
+    int occ[kBatchClasses][2] = {};  // resident CTAs per SM: batch class, SwiGLU (0: unknown)
+    int occ_cta[2][2] = {};          // single-call kernel (B = 1, 2; SwiGLU)
 };
 std::mutex g_dev_mutex;
 DeviceInfo g_dev[kMaxDevices];
@@ -620,18 +256,22 @@ bool device_info(DeviceInfo &out) {
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return false;
         d.sms = sms;
     }
-    const int v = variant();
     for (int bc = 0; bc < kBatchClasses; ++bc)
         for (int du = 0; du < 2; ++du) {
-            if (d.occ[v][bc][du] != 0) continue;
-            const KernelCfg k = kernel_cfg(v, class_batch(bc), du != 0);
-            if (k.smem > 48 * 1024 &&
-                cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem) != cudaSuccess)
-                return false;
+            if (d.occ[bc][du] != 0) continue;
+            const KernelCfg k = kernel_cfg(class_batch(bc), du != 0);
             int o = 0;
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k.fn, k.threads, k.smem) != cudaSuccess)
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k.fn, k.threads, 0) != cudaSuccess) return false;
+            d.occ[bc][du] = std::max(o, 1);
+        }
+    for (int bb = 0; bb < 2; ++bb)
+        for (int du = 0; du < 2; ++du) {
+            if (d.occ_cta[bb][du] != 0) continue;
+            int o = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, cta_kernel(bb + 1, du != 0), kThreads, 0) !=
+                cudaSuccess)
                 return false;
-            d.occ[v][bc][du] = std::max(o, 1);
+            d.occ_cta[bb][du] = std::max(o, 1);
         }
     out = d;
     return true;
@@ -656,18 +296,34 @@ Split make_split(int G, int requested) {
     return Split{(G + Gs - 1) / Gs, Gs};
 }
 
-// Selector: enough work items to give every resident warp about one item.
-// The warp count comes from the live occupancy of this build; the per-shape
-// tuning table is measured separately and can override it through cfg/env.
+// Work items in flight on the device: resident warps (batch-1 kernel) or CTAs
+// (tile path).
+long long resident_workers(int pb, bool dual, const DeviceInfo &d) {
+    return (long long)d.sms * d.occ[batch_class(pb)][dual] * kernel_cfg(pb, dual).warps;
+}
+
+// Selector of single calls.
+// B = 1..2 (q4rdna_gemv_cta.cuh): as many CTA K-ranges as fit in ONE wave of
+// resident CTAs (RB * S <= SMs x CTAs per SM), but at least one group per warp
+// (S <= G / 8).  Measured on B200 (bench.py --single --single-sweep, B = 1,
+// split 1..16, us per call), this rule picks the best split within 2% on every
+// config shape: 4096x4096 S = 8 (6.9 us; best 6.8 at S = 4), 12288x4096 S = 3
+// (9.9 us, the best), 4096x12288 S = 9 (10.3 us; best 10.1 at S = 8),
+// 1024x4096 S = 8 (5.5 us; best 5.4), gate+up 12288x4096 S = 3 (14.1 us, the
+// best).  A second wave costs up to 50%: 12288x4096 at S = 4 (384 CTAs)
+// 12.6 us, 4096x12288 at S = 10 (320 CTAs) 15.1 us.
+// B = 3..16 (the tile path): about one item per resident CTA.
 int select_split_for(int N, int K, int B, int op, const DeviceInfo &d) {
-    (void)op;
     const int G = K / Q4_GROUP;
     const int RB = (N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
-    const int pb = B;
     const bool dual = op == Q4RDNA_OP_SWIGLU;
-    const long long warps =
-        (long long)d.sms * d.occ[variant()][batch_class(pb)][dual] * kernel_cfg(variant(), pb, dual).warps;
-    long long S = (warps + RB - 1) / RB;
+    if (B < kTileMinBatch) {
+        const long long ctas = (long long)d.sms * d.occ_cta[B - 1][dual];
+        const long long S = std::min<long long>(ctas / RB, std::max(1, G / kWarps));
+        return make_split(G, (int)std::max<long long>(S, 1)).S;
+    }
+    const long long warps = resident_workers(B, dual, d);
+    const long long S = (warps + RB - 1) / RB;
     return make_split(G, (int)std::min<long long>(S, G)).S;
 }
 
@@ -714,16 +370,11 @@ size_t plan_ws_bytes_for(int N, int B, int S, int op, bool norm) {
 }
 
 // Work items per resident warp (or tile-path CTA) that a plan's split-K choice
-// aims at; Q4RDNA_PLAN_ITEMS overrides the default for A/B measurements.
-double plan_items_per_worker() {
-    const char *e = std::getenv("Q4RDNA_PLAN_ITEMS");
-    const double v = (e != nullptr && *e != '\0') ? std::atof(e) : 0.0;
-    return v > 0.0 ? std::min(v, 1024.0) : 2.0;
-}
-
-// The fused RMSNorm runs in the int8 batch-1 kernel and the tile path, not in
-// the A/B variants (Q4RDNA_KERNEL=ldg|i8tma).
-bool norm_supported(int B) { return B >= tile_min_batch() || variant() == kI8; }
+// aims at.  Every split costs partial stores, a fence, an arrival ticket and a
+// reduction per item, which on the Qwen3-8B step cost more than the imbalance
+// of large unsplit items (measured item sizes, one launch: 32 KB 1804 us,
+// 64 KB 949 us, 128 KB 703 us, 256 KB 656 us, unsplit 624-632 us).
+constexpr double kPlanItemsPerWorker = 2.0;
 
 bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
@@ -735,18 +386,18 @@ q4rdna_status check_shape(int N, int K, int B) {
 }
 
 int grid_for(long long items, int pb, bool dual, const DeviceInfo &d) {
-    const KernelCfg k = kernel_cfg(variant(), pb, dual);
+    const KernelCfg k = kernel_cfg(pb, dual);
     const long long want = (items + k.warps - 1) / k.warps;
-    const long long cap = (long long)d.sms * d.occ[variant()][batch_class(pb)][dual];
+    const long long cap = (long long)d.sms * d.occ[batch_class(pb)][dual];
     return (int)std::max<long long>(1, std::min(want, cap));
 }
 
 // pb: batch columns of the launch (1..16).
 q4rdna_status launch(const Launch &L, int grid, int pb, bool dual, cudaStream_t stream, bool norm = false) {
-    const KernelCfg k = kernel_cfg(variant(), pb, dual, norm);
+    const KernelCfg k = kernel_cfg(pb, dual, norm);
     Launch arg = L;
     void *args[] = {&arg};
-    if (cudaLaunchKernel(k.fn, dim3(grid), dim3(k.threads), args, (size_t)k.smem, stream) != cudaSuccess)
+    if (cudaLaunchKernel(k.fn, dim3(grid), dim3(k.threads), args, 0, stream) != cudaSuccess)
         return Q4RDNA_ERR_CUDA;
     if (cudaGetLastError() != cudaSuccess) return Q4RDNA_ERR_CUDA;
     g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -764,7 +415,6 @@ q4rdna_status gemv_common(int op, const uint8_t *w, const uint8_t *w2, const flo
     if (!aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(x, 8) || !aligned(y, 4) || (add && !aligned(add, 4)) ||
         (gn && !aligned(gn, 8)))
         return Q4RDNA_ERR_ALIGNMENT;
-    if (gn != nullptr && !norm_supported(B)) return Q4RDNA_ERR_UNSUPPORTED;
     DeviceInfo d;
     if (!device_info(d)) return Q4RDNA_ERR_DEVICE;
     const int G = K / Q4_GROUP;
@@ -800,6 +450,30 @@ q4rdna_status gemv_common(int op, const uint8_t *w, const uint8_t *w2, const flo
     T.nss = (gn != nullptr && sp.S > 1) ? part + partial_bytes(N, B, sp.S, op) / sizeof(float) : nullptr;
     L.total_items = (long long)RB * sp.S;
     const bool dual = op == Q4RDNA_OP_SWIGLU;
+    if (B < kTileMinBatch && gn == nullptr) {
+        // single call at B = 1..2: one CTA per (row block, K-range), K-range
+        // split over the CTA's warps (q4rdna_gemv_cta.cuh)
+        CtaArgs a;
+        a.T = T;
+        a.B = B;
+        a.Gw = (sp.Gs + kWarps - 1) / kWarps;
+        void *args[] = {&a};
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = dim3((unsigned)(RB * sp.S));
+        lc.blockDim = dim3(kThreads);
+        lc.stream = stream;
+        cudaLaunchAttribute at[1];
+        if (cfg != nullptr && (cfg->flags & Q4RDNA_CFG_OVERLAP_PREVIOUS)) {
+            at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            at[0].val.programmaticStreamSerializationAllowed = 1;
+            lc.attrs = at;
+            lc.numAttrs = 1;
+        }
+        if (cudaLaunchKernelExC(&lc, cta_kernel(B, dual), args) != cudaSuccess) return Q4RDNA_ERR_CUDA;
+        if (cudaGetLastError() != cudaSuccess) return Q4RDNA_ERR_CUDA;
+        g_launches.fetch_add(1, std::memory_order_relaxed);
+        return Q4RDNA_OK;
+    }
     return launch(L, grid_for(L.total_items, B, dual, d), B, dual, stream, gn != nullptr);
 }
 
@@ -815,6 +489,7 @@ struct GatherSignal {
     uint32_t *local;              // this rank's flag array
     int world, rank;
     uint32_t epoch;
+    int tries;                    // flag polls before the wait gives up (~0.5 us each)
 };
 constexpr int kGatherTries = 1 << 22;  // x ~0.5 us sleep: about 2 s
 constexpr unsigned kFaultGatherTimeout = 2u;
@@ -827,13 +502,13 @@ __global__ void q4_gather_signal_kernel(const __grid_constant__ GatherSignal a) 
     __threadfence_system();
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.peer[p] + a.rank), "r"(a.epoch) : "memory");
     int i = 0;
-    for (; i < kGatherTries; ++i) {
+    for (; i < a.tries; ++i) {
         uint32_t v;
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a.local + p) : "memory");
         if ((int)(v - a.epoch) >= 0) break;
         __nanosleep(500);
     }
-    if (i == kGatherTries) atomicOr(&g_fault, kFaultGatherTimeout);
+    if (i == a.tries) atomicOr(&g_fault, kFaultGatherTimeout);
 }
 
 // Segment counts.  Plan runs default to one launch: with the plan-wide split
@@ -1083,44 +758,18 @@ q4rdna_status plan_create_rdna(const q4rdna_gemv_desc *descs, int count, int B, 
     size_t ws_total = 0;
     long long items = 0;
     uint64_t wbytes = 0, abytes = 0;
-    // Split-K only as far as the whole plan needs it: every split adds partial
-    // stores, a fence and a reduction per item, which on the Qwen3-8B step cost
-    // more than the imbalance of unsplit items (624 us per step unsplit, 949 us
-    // with ~64 KB items).  Each task gets the split that gives the plan about
-    // plan_items_per_worker() items per resident warp (CTA on the tile path).
+    // Split-K only as far as the whole plan needs it: each task gets the split
+    // that gives the plan about kPlanItemsPerWorker items per resident warp
+    // (CTA on the tile path).
     long long total_rb = 0;
     bool any_dual_task = false;
     for (int i = 0; i < count; ++i) {
         if (descs[i].N > 0) total_rb += (descs[i].N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
         any_dual_task = any_dual_task || descs[i].op == Q4RDNA_OP_SWIGLU;
     }
-    const long long workers = (long long)d.sms * d.occ[variant()][batch_class(B)][any_dual_task] *
-                              kernel_cfg(variant(), B, any_dual_task).warps;
-    const double want_items = plan_items_per_worker() * (double)workers;
+    const long long workers = resident_workers(B, any_dual_task, d);
+    const double want_items = kPlanItemsPerWorker * (double)workers;
     const int plan_split = total_rb > 0 ? (int)std::max(1.0, std::ceil(want_items / (double)total_rb)) : 1;
-    // Tail split (Q4RDNA_TAIL_SPLIT = S > 1, A/B measurements): the tasks with
-    // the cheapest items, about one item per worker of them, are split S ways,
-    // so that the plan's last round (items run longest first) is made of
-    // smaller items.
-    std::vector<int> tail_req(count, 0);
-    if (const char *ts = std::getenv("Q4RDNA_TAIL_SPLIT")) {
-        const int S = std::atoi(ts);
-        if (S > 1 && plan_split == 1) {
-            std::vector<int> order(count);
-            for (int i = 0; i < count; ++i) order[i] = i;
-            auto cost = [&](int i) {
-                return (long long)(descs[i].K / Q4_GROUP) * (descs[i].op == Q4RDNA_OP_SWIGLU ? 2 : 1);
-            };
-            std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return cost(a) < cost(b); });
-            long long acc = 0;
-            for (int i : order) {
-                if (acc >= workers) break;
-                if (descs[i].split > 0 || descs[i].N <= 0) continue;
-                tail_req[i] = S;
-                acc += (long long)(descs[i].N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS * S;
-            }
-        }
-    }
     for (int i = 0; i < count; ++i) {
         const q4rdna_gemv_desc &e = descs[i];
         q4rdna_status st = check_shape(e.N, e.K, B);
@@ -1132,11 +781,10 @@ q4rdna_status plan_create_rdna(const q4rdna_gemv_desc *descs, int count, int B, 
         if (!aligned(e.tiles, 16) || (e.gate_tiles && !aligned(e.gate_tiles, 16)) || !aligned(e.x, 8) ||
             !aligned(e.y, 4) || (e.add && !aligned(e.add, 4)) || (e.norm_weight && !aligned(e.norm_weight, 8)))
             return Q4RDNA_ERR_ALIGNMENT;
-        if (e.norm_weight != nullptr && !norm_supported(B)) return Q4RDNA_ERR_UNSUPPORTED;
         const int planes = e.op == Q4RDNA_OP_SWIGLU ? 2 : 1;
         const int G = e.K / Q4_GROUP;
         const int RB = (e.N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
-        const int req = e.split > 0 ? e.split : std::min(tail_req[i] > 0 ? tail_req[i] : plan_split, G);
+        const int req = e.split > 0 ? e.split : std::min(plan_split, G);
         const Split sp = make_split(G, req);
         Task &T = host[i];
         T.w = e.tiles; T.w2 = e.gate_tiles; T.x = e.x; T.add = e.add; T.y = e.y;
@@ -1339,6 +987,7 @@ q4rdna_status q4rdna_plan_set_gather(q4rdna_plan *plan, int world, int rank, con
     sg.local = flags[rank];
     sg.world = world;
     sg.rank = rank;
+    if (sg.tries <= 0) sg.tries = kGatherTries;
     plan->epoch = 0;
     plan->gather = true;
     plan->seg_request = -1;  // segments are rebuilt with the gather's tables
@@ -1601,6 +1250,14 @@ q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *
 q4rdna_status q4rdna_plan_set_segments(q4rdna_plan *plan, int segments) {
     if (plan == nullptr || segments < 0) return Q4RDNA_ERR_INVALID_ARGUMENT;
     plan->run_segments = segments == 0 ? 1 : segments;
+    return Q4RDNA_OK;
+}
+
+q4rdna_status q4rdna_plan_set_gather_timeout(q4rdna_plan *plan, uint32_t microseconds) {
+    if (plan == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    // one poll is a flag load plus a ~0.5 us sleep hint
+    const uint64_t t = microseconds == 0 ? (uint64_t)kGatherTries : (uint64_t)microseconds * 2u;
+    plan->sig.tries = (int)std::min<uint64_t>(std::max<uint64_t>(t, 1), (uint64_t)1 << 30);
     return Q4RDNA_OK;
 }
 

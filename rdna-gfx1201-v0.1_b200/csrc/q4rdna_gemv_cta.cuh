@@ -1,0 +1,181 @@
+// Single-call GEMV for B = 1..2 (included into q4rdna_gemv.cu inside namespace
+// q4, after q4rdna_gemv_i8.cuh).
+//
+// A lone GEMV has too few rows to keep every warp busy with whole-K items: a
+// warp streams one group (4.3 KB) per DRAM round trip, so an item of 64 groups
+// takes ~60 us whatever the matrix size.  Here one CTA work item is one
+// 128-row block x one K-range of Gs groups, and the CTA's 8 warps split that
+// range again (Gw groups each), so the whole matrix is in flight at once:
+//   * every warp streams its groups through the batch-1 kernel's register
+//     pipeline and int8 MMAs (mma_step_i8), with its own activation prep;
+//   * the 8 warps' sums meet in shared memory, added in warp order;
+//   * with S > 1 CTA K-ranges, each CTA stores its partial sums to the
+//     workspace and the last CTA to arrive at the row block (arrival ticket)
+//     adds them in ascending order with all 256 threads and applies the add /
+//     SwiGLU epilogue.
+// Accumulation order of an output: exact int32 inside a group; the groups of a
+// warp in ascending order (as in the batch-1 kernel); warps in ascending order;
+// CTA K-ranges in ascending order.  Deterministic: no data atomics.
+//
+// Programmatic dependent launch (Q4RDNA_CFG_OVERLAP_PREVIOUS): every CTA lets
+// the next kernel of the stream launch at once, and waits for the previous
+// kernel (griddepcontrol.wait) after its first weight step is in flight and
+// before any read of x, the workspace or add and any store.  Launched without
+// the attribute, both instructions do nothing.
+
+struct CtaArgs {
+    Task T;  // T.S = CTA K-ranges, T.Gs = groups per K-range
+    int B;
+    int Gw;  // groups per warp
+};
+
+template <int BB>
+__device__ __forceinline__ void cta_fetch_x(const Task &T, int B, int g, int lane, float2 (&xv)[BB]) {
+#pragma unroll
+    for (int b = 0; b < BB; ++b)
+        xv[b] = b < B ? __ldg(reinterpret_cast<const float2 *>(T.x + (size_t)b * T.K + (size_t)g * Q4_GROUP) + lane)
+                      : make_float2(0.0f, 0.0f);
+}
+
+template <int BB, bool DUAL>
+__global__ void __launch_bounds__(kThreads, 2) q4_gemv_cta_kernel(const __grid_constant__ CtaArgs A) {
+    constexpr int planes = DUAL ? 2 : 1;
+    __shared__ I8X<BB> xsm[kWarps][2];
+    __shared__ float red[kWarps][planes][4][BB][32];
+    __shared__ unsigned last;
+    const Task &T = A.T;
+    const int B = A.B;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rb = blockIdx.x / T.S, sc = blockIdx.x % T.S;
+    const int gc1 = min((sc + 1) * T.Gs, T.G);
+    const int g0 = sc * T.Gs + warp * A.Gw;
+    const int ng = max(0, min(A.Gw, gc1 - g0));
+    const int grp = lane >> 2, c = lane & 3, t = grp >> 1, h = grp & 1;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    float acc[2][4][BB];
+#pragma unroll
+    for (int pl = 0; pl < 2; ++pl)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int b = 0; b < BB; ++b) acc[pl][q][b] = 0.0f;
+
+    if (ng > 0) {
+        I8Sel sel;
+        {
+            const int n = lane >> 2;  // this lane's B column
+            sel.a = sel_one(n >> 1, (n & 1) ? 0 : 1);
+            sel.b2 = sel_one(n >> 1, 2);
+            sel.b3 = sel_one(n >> 1, 3);
+            sel.bcol_odd = n & 1;
+        }
+        // rows past N read the block's first row tile (always present): every
+        // load stays in bounds, and those rows are never stored
+        int tile_row = rb * Q4_BLOCK_TILES + t;
+        if (tile_row >= (T.N >> 5)) tile_row = rb * Q4_BLOCK_TILES;
+        const size_t off = ((size_t)tile_row * T.G + g0) * Q4_TILE_BYTES;
+        const uint8_t *base0 = T.w + off;
+        const uint8_t *base1 = DUAL ? T.w2 + off : base0;
+        const int nsteps = ng * planes;
+        auto step_tile = [&](int st) -> const uint8_t * {
+            const int tt = DUAL ? (st & 1) : 0, gl = DUAL ? (st >> 1) : st;
+            return (tt ? base1 : base0) + (size_t)gl * Q4_TILE_BYTES;
+        };
+        I8X<BB>(&xs)[2] = xsm[warp];
+        StepBufI8 buf;
+        load_step_i8(buf, base0, c, h);  // weights: not written by the previous kernels
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        float2 xv[BB], gv = make_float2(1.0f, 1.0f);
+        cta_fetch_x<BB>(T, B, g0, lane, xv);
+#pragma unroll
+        for (int b = 0; b < BB; ++b) prep_group_i8<false>(xv[b], gv, false, xs[0].xq[b], &xs[0].up[b], &xs[0].ss[b], lane);
+        if (ng > 1) cta_fetch_x<BB>(T, B, g0 + 1, lane, xv);
+        __syncwarp();
+        int par = 0;
+        for (int st = 0; st < nsteps; ++st) {
+            const int tt = DUAL ? (st & 1) : 0, gl = DUAL ? (st >> 1) : st;
+            // the last step refills from its own tile (in bounds, never used)
+            RegSource src(buf, step_tile(st + 1 < nsteps ? st + 1 : st), c, h);
+            if (tt == 0) {
+                mma_step_i8<BB>(src, xs[par], acc[0], lane, sel);
+                if (gl + 1 < ng) {
+                    // the next group's activation into the other buffer
+#pragma unroll
+                    for (int b = 0; b < BB; ++b)
+                        prep_group_i8<false>(xv[b], gv, false, xs[par ^ 1].xq[b], &xs[par ^ 1].up[b],
+                                             &xs[par ^ 1].ss[b], lane);
+                    if (gl + 2 < ng) cta_fetch_x<BB>(T, B, g0 + gl + 2, lane, xv);
+                }
+            } else {
+                mma_step_i8<BB>(src, xs[par], acc[DUAL ? 1 : 0], lane, sel);
+            }
+            if (!DUAL || tt == 1) {
+                __syncwarp();
+                par ^= 1;
+            }
+        }
+    } else {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+    }
+
+    // the warps' sums meet in shared memory
+#pragma unroll
+    for (int pl = 0; pl < planes; ++pl)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int b = 0; b < BB; ++b) red[warp][pl][q][b][lane] = acc[pl][q][b];
+    __syncthreads();
+
+    // thread -> outputs (q, b, ln) of the block: row = tile (ln >> 3) of the
+    // block, row in tile 16 ((ln >> 2) & 1) + (ln & 3) + 4 q
+    constexpr int kOut = 4 * BB * 32;
+    const size_t split_stride = (size_t)planes * B * T.N;
+    for (int o = threadIdx.x; o < kOut; o += kThreads) {
+        const int ln = o & 31, b = (o >> 5) % BB, q = o / (32 * BB);
+        if (b >= B) continue;
+        const int lt = ln >> 3, lh = (ln >> 2) & 1, lc = ln & 3;
+        const int row = (rb * Q4_BLOCK_TILES + lt) * Q4_TILE_ROWS + 16 * lh + lc + 4 * q;
+        if (row >= T.N) continue;
+        float v[planes];
+#pragma unroll
+        for (int pl = 0; pl < planes; ++pl) {
+            float s = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) s += red[w][pl][q][b][ln];
+            v[pl] = s;
+        }
+        const size_t idx = (size_t)b * T.N + row;
+        if (T.S == 1) {
+            T.y[idx] = finish(v[0], v[planes - 1], T.op, T.add, idx);
+        } else {
+#pragma unroll
+            for (int pl = 0; pl < planes; ++pl) __stcg(&T.part[(size_t)sc * split_stride + (size_t)pl * B * T.N + idx], v[pl]);
+        }
+    }
+    if (T.S == 1) return;
+
+    // K-ranges of several CTAs: the last one to arrive adds them in order
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(&T.ticket[rb], 1u) == (unsigned)(T.S - 1) ? 1u : 0u;
+    __syncthreads();
+    if (last == 0) return;
+    __threadfence();
+    for (int o = threadIdx.x; o < Q4_BLOCK_ROWS * BB; o += kThreads) {
+        const int r = o % Q4_BLOCK_ROWS, b = o / Q4_BLOCK_ROWS;
+        const int row = rb * Q4_BLOCK_ROWS + r;
+        if (b >= B || row >= T.N) continue;
+        const size_t idx = (size_t)b * T.N + row;
+        float v[planes];
+#pragma unroll
+        for (int pl = 0; pl < planes; ++pl) {
+            float s = 0.0f;
+            for (int sp = 0; sp < T.S; ++sp) s += __ldcg(&T.part[(size_t)sp * split_stride + (size_t)pl * B * T.N + idx]);
+            v[pl] = s;
+        }
+        T.y[idx] = finish(v[0], v[planes - 1], T.op, T.add, idx);
+    }
+    if (threadIdx.x == 0) atomicExch(&T.ticket[rb], 0u);
+}

@@ -1,20 +1,24 @@
-// int8 tensor-core variant of the GEMV (included into q4rdna_gemv.cu inside
-// namespace q4).  Same work items and 128-bit load pattern as q4_gemv_kernel,
-// with fewer instructions per weight:
+// int8 tensor-core GEMV for B = 1..2 (included into q4rdna_gemv.cu inside
+// namespace q4).  A warp work item is one 128-row block (four 32-row tiles) x
+// one K-range of Gs groups; the warp streams its tiles with 128-bit loads
+// through a register pipeline.
 //
 //   * codes: a nibble in the HIGH half of a byte is exactly 16 * code as an s8,
 //     so a 32-bit code word (4 rows x 2 columns) becomes two A registers with
 //     hi = w & 0xF0F0F0F0 and lo = (w << 4) & 0xF0F0F0F0: 3 integer ops per 8
 //     weights, no conversion and no offset to undo;
 //   * activation: per group, x is scaled by a power of two so its largest
-//     magnitude lies in [2^21, 2^22), rounded to an integer X (error <= 2^-22 of
-//     the group's largest |x|) and used as its own bytes,
-//     X = B2 * 65536 + B1 * 256 + B0 with B0, B1 unsigned and B2 = X >> 16
-//     signed: no limb arithmetic;
-//   * mma.sync m16n8k32 s8 x u8 (bytes 0, 1) and s8 x s8 (byte 2) -> s32 sum
-//     the products of one group exactly; the epilogue combines the byte sums in
-//     f32 and applies scale * 2^e / 16 once per (row, group), as the reference
-//     applies its scale (q4rdna.cu:370-371).
+//     magnitude lies in [2^29, 2^30) and rounded to an integer X, so every
+//     element keeps an absolute error <= 2^-30 of the group's largest |x|.  X is
+//     written in four balanced base-256 digits, X = d3 2^24 + d2 2^16 + d1 2^8
+//     + d0 with every d in [-128, 127]: the digit word is
+//     (X + 0x808080) ^ 0x808080 read as four s8 bytes (bytes 0..2 are the
+//     biased digits d + 128 with the XOR undoing the bias; byte 3 absorbs the
+//     carries);
+//   * mma.sync m16n8k32 s8 x s8 -> s32 sums the products of one group exactly
+//     per digit; the epilogue combines the digit sums in f32 and applies
+//     scale * 2^e / 16 once per (row, group), as the reference applies its
+//     scale (q4rdna.cu:370-371).
 //
 // Fragment mapping (m16n8k32, A row-major, B col-major).  Lane (grp, c) loads,
 // for k-step m, 16 bytes of tile t = grp >> 1 at 64 + 128m + 32c + 16h
@@ -22,19 +26,22 @@
 // i = 4m + c.  Row set r (r = 0, 1) uses q[2r] for MMA row grp and q[2r+1] for
 // MMA row grp + 8: A k-slots 4c + j hold the low-nibble column 2i of row
 // (16h + 8r + j [+4]), k-slots 16 + 4c + j the high-nibble column 2i + 1.  The
-// four rows of a register are separated by the B operand: for "MMA a" (u8)
-// column n = 2 * slot + q carries byte B1 (q = 0) or B0 (q = 1) of X placed in
-// byte `slot` of the B register; for "MMA b" (s8) column 2 * slot + bb carries
-// B2 of batch column 2p + bb.  So lane (grp, c) ends up holding, without any
-// shuffle, all three byte sums of rows 16h + c + {0, 4, 8, 12} of tile t.
-// Accumulation order: exact int32 inside a group; groups of a split in
-// ascending order as sum = fma(scale / 16, (hi_limbs + lo_limbs) * 2^e, sum);
+// four rows of a register are separated by the B operand: for "MMA a" column
+// n = 2 * slot + q carries digit d1 (q = 0) or d0 (q = 1) of X placed in byte
+// `slot` of the B register; for "MMA b" column 2 * slot + bb carries d2 of batch
+// column bb, and for BB = 1 (where bb = 1 is free) d3 of column 0 instead; at
+// BB = 2 "MMA c" carries d3 the way "MMA b" carries d2.  So lane (grp, c) ends
+// up holding, without any shuffle, all four digit sums of rows
+// 16h + c + {0, 4, 8, 12} of tile t.
+// Accumulation order: exact int32 inside a group per digit; the digit sums
+// recombined as ((S0 + 256 S1) + 2^16 S2) + 2^24 S3 (three f32 roundings);
+// groups of a split in ascending order as sum = fma(scale / 16, v * 2^e, sum);
 // splits in ascending order in f32 (finish_rows).
 
 // One group of the activation, ready for the B operand.
 template <int BB>
 struct __align__(16) I8X {
-    uint32_t xq[BB][Q4_GROUP];  // per k: the integer X (bytes B0, B1, B2 used)
+    uint32_t xq[BB][Q4_GROUP];  // per k: the four balanced digits of X (one s8 each)
     float up[BB];               // 2^e: undoes the group's power-of-two scaling
     float ss[BB];               // fused RMSNorm: the group's sum of h^2
 };
@@ -46,6 +53,17 @@ __device__ __forceinline__ float warp_sum(float v) {
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
 }
+
+// Activation scaling shared by both int8 kernels.  E = biased exponent of the
+// group's largest |x| = m, clamped to >= 30 so that both 2^(156 - E) and
+// 2^(E - 156) are normal f32 numbers: m * 2^(156 - E) lies in [2^29, 2^30), so
+// |X| <= 2^30 after rounding.  Groups whose largest |x| is below 2^-97 lose
+// bits to the clamp.
+__device__ __forceinline__ uint32_t act_exponent(float m) { return max((__float_as_uint(m) >> 23) & 0xffu, 30u); }
+__device__ __forceinline__ float act_scale(uint32_t e) { return __uint_as_float((283u - e) << 23); }   // 2^(156 - E)
+__device__ __forceinline__ float act_unscale(uint32_t e) { return __uint_as_float((e - 29u) << 23); }  // 2^(E - 156)
+// X (|X| <= 2^30) -> its four balanced base-256 digits as s8 bytes.
+__device__ __forceinline__ uint32_t act_digits(int X) { return ((uint32_t)X + 0x00808080u) ^ 0x00808080u; }
 
 // NORM kernels: v is the raw RMSNorm input h and gv the norm weight of the same
 // columns (1 for the launch's tasks without a norm); the group is prepared as
@@ -71,23 +89,21 @@ __device__ __forceinline__ void prep_group_i8(float2 v, float2 gv, bool norm, ui
     } else {
         m = warp_max(fmaxf(fabsf(v.x), fabsf(v.y)));
     }
-    // biased exponent E of the max: scale by 2^(148 - E) so max*scale < 2^22.
-    // E >= 22 keeps both 2^(148 - E) and 2^(E - 148) normal f32 numbers; only
-    // groups whose largest |x| is below 2^-104 lose bits to the clamp.
-    const uint32_t e = max((__float_as_uint(m) >> 23) & 0xffu, 22u);
+    const uint32_t e = act_exponent(m);
     const bool nz = m > 0.0f;
-    const float f = nz ? __uint_as_float((275u - e) << 23) : 1.0f;
-    const float u = nz ? __uint_as_float((e - 21u) << 23) : 1.0f;
+    const float f = nz ? act_scale(e) : 1.0f;
+    const float u = nz ? act_unscale(e) : 1.0f;
     uint2 w;
-    w.x = (uint32_t)__float2int_rn(v.x * f);  // |X| < 2^22: byte 2 as s8 is X >> 16
-    w.y = (uint32_t)__float2int_rn(v.y * f);
+    w.x = act_digits(__float2int_rn(v.x * f));
+    w.y = act_digits(__float2int_rn(v.y * f));
     reinterpret_cast<uint2 *>(xq_row)[lane] = w;
     if (lane == 0) *up = u;
 }
 
 // An int32 sum S with |S| < 2^22 accumulated on top of kMagicI reads, as f32
 // bits, 1.5 * 2^23 + S exactly: the int -> float conversion becomes one
-// subtraction (or one fma with a scaled bias) on the full-rate pipe.
+// subtraction (or one fma with a scaled bias) on the full-rate pipe.  A digit
+// sum of one group is at most 64 * 128 * 128 = 2^20 in magnitude.
 constexpr int kMagicI = 0x4B400000;
 constexpr float kMagicF = 12582912.0f;  // 1.5 * 2^23
 
@@ -99,34 +115,27 @@ __device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1,
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Same with unsigned B bytes.
-__device__ __forceinline__ void imma16832_u(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                            uint32_t b0, uint32_t b1) {
-    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-// Number of "MMA a" and "MMA b" instructions (B2 of two batch columns each) for BB columns.
+// Number of "MMA a" (d1, d0 of one batch column) and of high-digit MMAs: at
+// BB = 1 one MMA carries d2 and d3; at BB = 2 "MMA b" carries d2 and "MMA c"
+// d3 of the batch pair.
 template <int BB>
 struct I8Shape {
-    static constexpr int NA = BB;             // "MMA a": B1, B0 of one batch column
-    static constexpr int NBP = (BB + 1) / 2;  // "MMA b": B2 of a batch pair
+    static constexpr int NA = BB;
+    static constexpr int NH = BB == 1 ? 1 : 2;
 };
 
 // B-operand selectors of this lane (fixed per kernel): byte `slot` of the
-// register takes byte `src` of the per-k word X; all other bytes are zero.
+// register takes byte `src` of the per-k digit word; all other bytes are zero.
 struct I8Sel {
-    uint32_t a;      // MMA a: src 1 (B1) or 0 (B0)
-    uint32_t b;      // MMA b: src 2 (B2), or all-zero when the batch is absent
-    int bcol_odd;    // MMA b: this lane's column carries batch 2p + 1
+    uint32_t a;      // MMA a: digit 1 or 0
+    uint32_t b2;     // high MMAs: digit 2 in byte `slot`
+    uint32_t b3;     // high MMAs: digit 3 in byte `slot`
+    int bcol_odd;    // high MMAs: this lane's column is odd (bb = 1)
 };
 
 __device__ __forceinline__ uint32_t sel_one(int slot, int src) {
     return (0x4444u & ~(0xFu << (4 * slot))) | ((uint32_t)src << (4 * slot));
 }
-
 // Code and scale words of one (tensor, group) step for this lane.
 struct StepBufI8 {
     uint4 q[8];     // k-step m: 16 code bytes
@@ -184,26 +193,27 @@ struct SmemSource {
     __device__ __forceinline__ uint4 codes(int m) { return *reinterpret_cast<const uint4 *>(q + 128 * m); }
 };
 
-// One group of one tensor: 16 (BB = 1) int8 MMAs per warp, exact int32 sums,
-// then the per-(row, group) scale in f32.
+// One group of one tensor: 32 (BB = 1) int8 MMAs per warp, exact int32 digit
+// sums, then the per-(row, group) scale in f32.
 template <int BB, class Src>
 __device__ __forceinline__ void mma_step_i8(Src &src, const I8X<BB> &sm, float (&acc)[4][BB], int lane,
                                             const I8Sel &sel) {
-    constexpr int NA = I8Shape<BB>::NA, NBP = I8Shape<BB>::NBP;
-    int D[2][NA + NBP][4];
+    constexpr int NA = I8Shape<BB>::NA, NH = I8Shape<BB>::NH;
+    int D[2][NA + NH][4];
 #pragma unroll
     for (int r = 0; r < 2; ++r)
 #pragma unroll
-        for (int k = 0; k < NA + NBP; ++k)
+        for (int k = 0; k < NA + NH; ++k)
 #pragma unroll
             for (int e = 0; e < 4; ++e) D[r][k][e] = kMagicI;  // read back as f32 with one add
     uint32_t sw[4];
     src.scales(sw);
     const int c4 = lane & 3;
+    const bool odd = sel.bcol_odd != 0;
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
         const uint4 cur = src.codes(m);
-        uint32_t ba0[NA], ba1[NA], bb0[NBP], bb1[NBP];
+        uint32_t ba0[NA], ba1[NA], bh0[NH], bh1[NH];
         uint2 W[BB];
 #pragma unroll
         for (int b = 0; b < BB; ++b) W[b] = *reinterpret_cast<const uint2 *>(&sm.xq[b][8 * m + 2 * c4]);
@@ -212,15 +222,20 @@ __device__ __forceinline__ void mma_step_i8(Src &src, const I8X<BB> &sm, float (
             ba0[b] = __byte_perm(W[b].x, 0u, sel.a);
             ba1[b] = __byte_perm(W[b].y, 0u, sel.a);
         }
+        if (BB == 1) {
+            // even columns: d2, odd columns: d3, both of batch column 0
+            const uint32_t s = odd ? sel.b3 : sel.b2;
+            bh0[0] = __byte_perm(W[0].x, 0u, s);
+            bh1[0] = __byte_perm(W[0].y, 0u, s);
+        } else {
+            // even columns: batch 0, odd columns: batch 1; MMA b d2, MMA c d3
+            const uint2 w = W[BB > 1 && odd ? 1 : 0];
 #pragma unroll
-        for (int p = 0; p < NBP; ++p) {
-            // compile-time indices; the lane's odd/even column picks by select
-            const uint2 we = W[2 * p];
-            const uint2 wo = W[2 * p + 1 < BB ? 2 * p + 1 : 2 * p];
-            const bool odd = sel.bcol_odd != 0;
-            const uint32_t s = (odd && 2 * p + 1 >= BB) ? 0x4444u : sel.b;
-            bb0[p] = __byte_perm(odd ? wo.x : we.x, 0u, s);
-            bb1[p] = __byte_perm(odd ? wo.y : we.y, 0u, s);
+            for (int p = 0; p < NH; ++p) {
+                const uint32_t s = p == 0 ? sel.b2 : sel.b3;
+                bh0[p] = __byte_perm(w.x, 0u, s);
+                bh1[p] = __byte_perm(w.y, 0u, s);
+            }
         }
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
@@ -231,25 +246,27 @@ __device__ __forceinline__ void mma_step_i8(Src &src, const I8X<BB> &sm, float (
             const uint32_t a2 = wa & 0xF0F0F0F0u;         // 16 * high-nibble code (column 2i + 1)
             const uint32_t a3 = wb & 0xF0F0F0F0u;
 #pragma unroll
-            for (int b = 0; b < NA; ++b) imma16832_u(D[r][b], a0, a1, a2, a3, ba0[b], ba1[b]);
+            for (int b = 0; b < NA; ++b) imma16832(D[r][b], a0, a1, a2, a3, ba0[b], ba1[b]);
 #pragma unroll
-            for (int p = 0; p < NBP; ++p) imma16832(D[r][NA + p], a0, a1, a2, a3, bb0[p], bb1[p]);
+            for (int p = 0; p < NH; ++p) imma16832(D[r][NA + p], a0, a1, a2, a3, bh0[p], bh1[p]);
         }
     }
-    // rows 16h + c + 4q, q = 2r + half: byte sums S1 = Da[2*half], S0 = Da[2*half+1],
-    // S2 = Db[2*half + (b & 1)]
+    // rows 16h + c + 4q, q = 2r + half: digit sums S1 = Da[2*half], S0 = Da[2*half+1];
+    // BB = 1: S2 = Dh[2*half], S3 = Dh[2*half+1]; BB = 2: S2 = Db[2*half + b], S3 = Dc[2*half + b]
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
         const int r = q >> 1, hf = q & 1;
         const float sc = __half2float(__ushort_as_half((unsigned short)sw[q])) * 0.0625f;
 #pragma unroll
         for (int b = 0; b < BB; ++b) {
-            // byte sums over kMagicI (|S| <= 64 * 128 * 255 < 2^22): S1 * 256 and
-            // S2 * 65536 come out of the fma exactly; v rounds once per add
+            const int d2 = BB == 1 ? D[r][NA][2 * hf] : D[r][NA][2 * hf + b];
+            const int d3 = BB == 1 ? D[r][NA][2 * hf + 1] : D[r][NA + 1][2 * hf + b];
+            // digit sums over kMagicI (|S| <= 2^20): S1 * 2^8, S2 * 2^16 and
+            // S3 * 2^24 come out of the fmas exactly; v rounds once per add
             const float s0 = __int_as_float(D[r][b][2 * hf + 1]) - kMagicF;
             const float lo = fmaf(__int_as_float(D[r][b][2 * hf]), 256.0f, -256.0f * kMagicF) + s0;
-            const float v =
-                fmaf(__int_as_float(D[r][NA + (b >> 1)][2 * hf + (b & 1)]), 65536.0f, -65536.0f * kMagicF) + lo;
+            const float mid = fmaf(__int_as_float(d2), 65536.0f, -65536.0f * kMagicF) + lo;
+            const float v = fmaf(__int_as_float(d3), 16777216.0f, -16777216.0f * kMagicF) + mid;
             // v * 2^e is exact (a power of two, in range), so this is one rounding
             acc[q][b] = fmaf(sc, v * sm.up[b], acc[q][b]);
         }
@@ -468,7 +485,8 @@ __global__ void __launch_bounds__(kThreads, BB <= 2 ? 2 : 1) q4_gemv_i8_kernel(c
     {
         const int n = lane >> 2;  // this lane's B column
         sel.a = sel_one(n >> 1, (n & 1) ? 0 : 1);
-        sel.b = sel_one(n >> 1, 2);
+        sel.b2 = sel_one(n >> 1, 2);
+        sel.b3 = sel_one(n >> 1, 3);
         sel.bcol_odd = n & 1;
     }
     const int c = lane & 3, h = (lane >> 2) & 1;

@@ -18,19 +18,19 @@
 //   * MMA row g <-> tile row 4g + 2 rs, MMA row g + 8 <-> 4g + 2 rs + 1
 //     (row set rs = 0, 1); k-slot 4c + j <-> column 2 P_j, k-slot 16 + 4c + j
 //     <-> column 2 P_j + 1;
-//   * the activation of one group, scaled by 2^(148 - E) (E = biased exponent
+//   * the activation of one group, scaled by 2^(156 - E) (E = biased exponent
 //     of the group's largest |x|, per batch column, as in the batch-1 kernel)
-//     and rounded to an integer X with |X| < 2^22, is used as its own three
-//     bytes: X = B2 * 65536 + B1 * 256 + B0 with B0, B1 unsigned (u8 operands)
-//     and B2 = X >> 16 signed (s8): no limb arithmetic at all.  The n-tiles are
-//     byte-major: n-tile t = limb * NBB + bb holds byte `limb` of batch columns
-//     8 bb .. 8 bb + 7.  The whole CTA prepares the B fragments of a chunk of
-//     groups once, in shared memory, for its four warps;
-//   * per group the int32 sums are exact (accumulated over a float bias, so
-//     that reading them as f32 costs one add: kMagicI); the epilogue combines
-//     them as S2 * 65536 + (S1 * 256 + S0), rounding once per add, and
-//     accumulates fma(scale / 16, v * 2^e, acc) in f32, groups in ascending
-//     order; splits are added in ascending order (mb_finish).
+//     and rounded to an integer X with |X| <= 2^30, is used as its four
+//     balanced base-256 digits (act_digits: X = d3 2^24 + d2 2^16 + d1 2^8 +
+//     d0, every digit an s8).  The n-tiles are digit-major: n-tile
+//     t = limb * NBB + bb holds digit `limb` of batch columns 8 bb .. 8 bb + 7.
+//     The whole CTA prepares the B fragments of a chunk of groups once, in
+//     shared memory, for its four warps;
+//   * per group the int32 digit sums are exact (accumulated over a float bias,
+//     so that reading them as f32 costs one add: kMagicI); the epilogue
+//     combines them as ((S0 + 2^8 S1) + 2^16 S2) + 2^24 S3, rounding once per
+//     add, and accumulates fma(scale / 16, v * 2^e, acc) in f32, groups in
+//     ascending order; splits are added in ascending order (mb_finish).
 //
 // Pipeline: the code words of chunk q + 1 are loaded into a slot's registers
 // as soon as that slot of chunk q is consumed, the activations of chunk q + 1
@@ -40,7 +40,7 @@
 template <int BP>
 struct MbShape {
     static constexpr int NBB = BP / 8;          // batch blocks of 8 columns
-    static constexpr int NT = 3 * NBB;          // n-tiles (byte-major)
+    static constexpr int NT = 4 * NBB;          // n-tiles (digit-major)
     static constexpr int SLOTS = 4;             // tile slots per chunk (groups x planes)
     static constexpr int GPP = 128 / (8 * BP);  // groups prepared per pass of 128 threads
     static constexpr int PASSES = 4 / GPP;
@@ -71,34 +71,21 @@ __device__ __forceinline__ void transpose4(uint32_t w0, uint32_t w1, uint32_t w2
 __device__ __forceinline__ uint32_t s8_hi(uint32_t w) { return w & 0xF0F0F0F0u; }
 __device__ __forceinline__ uint32_t s8_lo(uint32_t w) { return (w << 4) & 0xF0F0F0F0u; }
 
-// D (+)= A (s8) * B, B unsigned (U = true) or signed bytes; Z: the accumulator
-// starts at kMagicI (q4rdna_gemv_i8.cuh) instead of D.
-template <bool U, bool Z>
+// D (+)= A (s8) * B (s8); Z: the accumulator starts at kMagicI
+// (q4rdna_gemv_i8.cuh) instead of D.
+template <bool Z>
 __device__ __forceinline__ void imma_mb(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                         uint32_t b1) {
-    if (Z) {
-        if (U)
-            asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                "{%10,%10,%10,%10};"
-                : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(kMagicI));
-        else
-            asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                "{%10,%10,%10,%10};"
-                : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(kMagicI));
-    } else {
-        if (U)
-            asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                "{%0,%1,%2,%3};"
-                : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-        else
-            asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                "{%0,%1,%2,%3};"
-                : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-    }
+    if (Z)
+        asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%10,%10,%10,%10};"
+            : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(kMagicI));
+    else
+        asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 // Code words and scales of one tile for this lane.
@@ -248,20 +235,20 @@ __device__ __forceinline__ void mb_prep(MbSmem<BP> &sm, int par, const MbCursor 
             if (NORM) ssq += __shfl_xor_sync(0xffffffffu, ssq, o);
         }
         if (NORM && gi < c.ncg && (r & 7) == 0) sm.ss[par][gi][b] = ssq;
-        const uint32_t e = max((__float_as_uint(m) >> 23) & 0xffu, 22u);  // as prep_group_i8
+        const uint32_t e = act_exponent(m);  // as prep_group_i8
         const bool nz = m > 0.0f;
-        const float f = nz ? __uint_as_float((275u - e) << 23) : 1.0f;
-        const float u = nz ? __uint_as_float((e - 21u) << 23) : 1.0f;
+        const float f = nz ? act_scale(e) : 1.0f;
+        const float u = nz ? act_unscale(e) : 1.0f;
         uint32_t p0[4], p1[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            p0[j] = (uint32_t)__float2int_rn(v[j].x * f);
-            p1[j] = (uint32_t)__float2int_rn(v[j].y * f);
+            p0[j] = act_digits(__float2int_rn(v[j].x * f));
+            p1[j] = act_digits(__float2int_rn(v[j].y * f));
         }
         if (gi < c.ncg) {
             const int lane = (b & 7) * 4 + cc, bb = b >> 3;
 #pragma unroll
-            for (int limb = 0; limb < 3; ++limb) {
+            for (int limb = 0; limb < 4; ++limb) {
                 uint2 w;
                 w.x = gather_byte(p0[0], p0[1], p0[2], p0[3], limb);
                 w.y = gather_byte(p1[0], p1[1], p1[2], p1[3], limb);
@@ -296,14 +283,8 @@ __device__ __forceinline__ void mb_tile(const MbTileRegs &r, const MbSmem<BP> &s
             const uint2 bf = sm.b[par][gi][t][ks][lane];
 #pragma unroll
             for (int rs = 0; rs < 2; ++rs) {
-                const bool u8 = t < 2 * S::NBB;  // bytes 0, 1 of X are unsigned
-                if (ks == 0) {
-                    if (u8) imma_mb<true, true>(D[rs][t], A[rs][0], A[rs][1], A[rs][2], A[rs][3], bf.x, bf.y);
-                    else imma_mb<false, true>(D[rs][t], A[rs][0], A[rs][1], A[rs][2], A[rs][3], bf.x, bf.y);
-                } else {
-                    if (u8) imma_mb<true, false>(D[rs][t], A[rs][0], A[rs][1], A[rs][2], A[rs][3], bf.x, bf.y);
-                    else imma_mb<false, false>(D[rs][t], A[rs][0], A[rs][1], A[rs][2], A[rs][3], bf.x, bf.y);
-                }
+                if (ks == 0) imma_mb<true>(D[rs][t], A[rs][0], A[rs][1], A[rs][2], A[rs][3], bf.x, bf.y);
+                else imma_mb<false>(D[rs][t], A[rs][0], A[rs][1], A[rs][2], A[rs][3], bf.x, bf.y);
             }
         }
     }
@@ -323,13 +304,15 @@ __device__ __forceinline__ void mb_tile(const MbTileRegs &r, const MbSmem<BP> &s
 #pragma unroll
                 for (int q = 0; q < 2; ++q) {
                     const int k = 2 * e + q;
-                    // byte sums S0, S1, S2 (|S| <= 64 * 128 * 255 < 2^22) over kMagicI;
-                    // S1 * 256 and S2 * 65536 come out of the fma exactly, so v is
-                    // S2 * 65536 + S1 * 256 + S0 with two roundings
+                    // digit sums S0..S3 (|S| <= 2^20) over kMagicI; S1 * 2^8,
+                    // S2 * 2^16 and S3 * 2^24 come out of the fmas exactly, so v is
+                    // ((S0 + 2^8 S1) + 2^16 S2) + 2^24 S3 with three roundings
                     const float s0 = __int_as_float(D[rs][bb][k]) - kMagicF;
                     const float lo = fmaf(__int_as_float(D[rs][S::NBB + bb][k]), 256.0f, -256.0f * kMagicF) + s0;
-                    const float v =
+                    const float mid =
                         fmaf(__int_as_float(D[rs][2 * S::NBB + bb][k]), 65536.0f, -65536.0f * kMagicF) + lo;
+                    const float v =
+                        fmaf(__int_as_float(D[rs][3 * S::NBB + bb][k]), 16777216.0f, -16777216.0f * kMagicF) + mid;
                     acc[2 * rs + e][bb][q] = fmaf(s[2 * rs + e], v * (q ? uq.y : uq.x), acc[2 * rs + e][bb][q]);
                 }
     }

@@ -14,7 +14,9 @@
 // Host code must not pass the array's name to a kernel: on the host that name
 // is only a stand-in, not a device address.  The device address is looked up
 // once per device with cudaGetSymbolAddress, with that device current, on the
-// first call made on it.
+// first call made on it.  A device reset (cudaDeviceReset) reloads the module
+// and can move the array, so q4rdna_registry_reset also forgets the cached
+// addresses (noalloc_forget_devices); call it after a reset.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -50,6 +52,12 @@ q4rdna_status scratch_for_current_device(void **out) {
 }
 
 }  // namespace
+
+// Drops the cached device addresses (called by q4rdna_registry_reset).
+void noalloc_forget_devices() {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    for (void *&p : g_scratch_addr) p = nullptr;
+}
 
 extern "C" q4rdna_status q4rdna_gemv_noalloc(const uint8_t *tiles, const float *x, float *y, int N, int K, int B,
                                               const q4rdna_cfg *cfg, q4rdna_stream_t stream) {

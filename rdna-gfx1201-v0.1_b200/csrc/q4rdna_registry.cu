@@ -235,8 +235,12 @@ bool in_scope(const char *name) {
     return true;
 }
 
-// Loads on first use onto the current device; null if disabled.
-q4rdna_sidecar *ensure_loaded(Registry &r) {
+void *stream_workspace(Registry &r, cudaStream_t stream);
+
+// Loads on first use onto the current device; null if disabled.  The split-K
+// workspace of the calling stream is allocated in the same one-time load, next
+// to the weights, so later hook calls on that stream allocate nothing.
+q4rdna_sidecar *ensure_loaded(Registry &r, cudaStream_t stream) {
     if (r.attempted) return r.sc;
     r.attempted = true;
     const char *path = sidecar_path();
@@ -251,17 +255,26 @@ q4rdna_sidecar *ensure_loaded(Registry &r) {
     }
     size_t ws = 0;
     for (const Entry &e : sc->entries)
-        ws = std::max(ws, q4rdna_workspace_bytes((int)e.rows, (int)e.cols, 1, Q4RDNA_OP_SWIGLU, nullptr));
+        for (int op = Q4RDNA_OP_PLAIN; op <= Q4RDNA_OP_SWIGLU; ++op)
+            ws = std::max(ws, q4rdna_workspace_bytes((int)e.rows, (int)e.cols, 1, op, nullptr));
     r.ws_bytes = ws;
     r.sc = sc;
+    if (ws > 0 && stream_workspace(r, stream) == nullptr) {
+        std::fprintf(stderr, "Q4_RDNA: cannot allocate the %zu-byte split-K workspace\n", ws);
+        q4rdna_sidecar_close(sc);
+        r.sc = nullptr;
+        return nullptr;
+    }
     if (!g_atexit.exchange(true)) std::atexit(q4rdna_report_stats);
     std::fprintf(stderr, "Q4_RDNA: loaded %d tensors, %.2f GiB on device %d from %s\n", (int)sc->entries.size(),
                  double(sc->data_bytes) / (1024.0 * 1024.0 * 1024.0), dev, path);
     return sc;
 }
 
-// Workspace of one stream, allocated and zeroed on its first use (so the first
-// call on a stream must not be inside a graph capture).
+// Workspace of one stream: the loading stream's comes with the load; any other
+// stream's is allocated and zeroed on its first call (so the first call on a
+// stream must not be inside a graph capture).  All are freed by
+// q4rdna_registry_reset.
 void *stream_workspace(Registry &r, cudaStream_t stream) {
     if (r.ws_bytes == 0) return nullptr;
     auto it = r.ws.find(stream);
@@ -279,9 +292,9 @@ struct Found {
 };
 
 // q4rdna_find (source/q4rdna.cu:682-705): scope, lazy load, device, name, shape.
-bool find(Registry &r, const char *name, int64_t ne0, int64_t ne1, Found &out) {
+bool find(Registry &r, const char *name, int64_t ne0, int64_t ne1, cudaStream_t stream, Found &out) {
     if (name == nullptr || sidecar_path() == nullptr || !in_scope(name)) return false;
-    q4rdna_sidecar *sc = ensure_loaded(r);
+    q4rdna_sidecar *sc = ensure_loaded(r, stream);
     if (sc == nullptr) return false;
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev != sc->device) return false;
@@ -296,6 +309,24 @@ bool find(Registry &r, const char *name, int64_t ne0, int64_t ne1, Found &out) {
 
 }  // namespace
 
+void noalloc_forget_devices();  // q4rdna_noalloc.cu
+
+namespace {
+// Launch options of the hooks: the sidecar's tiles are written once at load and
+// never again, so each GEMV may start streaming them while the previous kernel
+// on the stream finishes (Q4RDNA_CFG_OVERLAP_PREVIOUS).  LLAMA_Q4_RDNA_OVERLAP=0
+// turns that off.
+const q4rdna_cfg *hook_cfg() {
+    static const q4rdna_cfg c = [] {
+        q4rdna_cfg v{};
+        const char *e = std::getenv("LLAMA_Q4_RDNA_OVERLAP");
+        v.flags = (e != nullptr && std::strcmp(e, "0") == 0) ? 0 : Q4RDNA_CFG_OVERLAP_PREVIOUS;
+        return v;
+    }();
+    return &c;
+}
+}  // namespace
+
 extern "C" {
 
 int q4rdna_mul_mat(const char *weight_name, int64_t weight_ne0, int64_t weight_ne1, const float *x, int64_t x_ne0,
@@ -304,14 +335,14 @@ int q4rdna_mul_mat(const char *weight_name, int64_t weight_ne0, int64_t weight_n
     Registry &r = registry();
     std::lock_guard<std::mutex> lock(r.mu);
     Found f;
-    if (!find(r, weight_name, weight_ne0, weight_ne1, f)) return 0;
+    if (!find(r, weight_name, weight_ne0, weight_ne1, (cudaStream_t)stream, f)) return 0;
     if (x_ne0 != (int64_t)f.entry->cols || y_ne0 != (int64_t)f.entry->rows) {
         std::fprintf(stderr, "Q4_RDNA: shape mismatch for %s\n", weight_name);
         return 0;
     }
     void *ws = stream_workspace(r, (cudaStream_t)stream);
     if (r.ws_bytes && ws == nullptr) return 0;
-    if (q4rdna_gemv(f.tiles, x, y, (int)f.entry->rows, (int)f.entry->cols, 1, nullptr, ws, r.ws_bytes, stream) !=
+    if (q4rdna_gemv(f.tiles, x, y, (int)f.entry->rows, (int)f.entry->cols, 1, hook_cfg(), ws, r.ws_bytes, stream) !=
         Q4RDNA_OK)
         return 0;
     g_op_launches.fetch_add(1, std::memory_order_relaxed);
@@ -326,13 +357,13 @@ int q4rdna_mul_mat_add(const char *weight_name, int64_t weight_ne0, int64_t weig
     Registry &r = registry();
     std::lock_guard<std::mutex> lock(r.mu);
     Found f;
-    if (!find(r, weight_name, weight_ne0, weight_ne1, f)) return 0;
+    if (!find(r, weight_name, weight_ne0, weight_ne1, (cudaStream_t)stream, f)) return 0;
     if (x_ne0 != (int64_t)f.entry->cols || add_nelements != (int64_t)f.entry->rows ||
         y_nelements != (int64_t)f.entry->rows)
         return 0;
     void *ws = stream_workspace(r, (cudaStream_t)stream);
     if (r.ws_bytes && ws == nullptr) return 0;
-    if (q4rdna_gemv_add(f.tiles, x, add, y, (int)f.entry->rows, (int)f.entry->cols, 1, nullptr, ws, r.ws_bytes,
+    if (q4rdna_gemv_add(f.tiles, x, add, y, (int)f.entry->rows, (int)f.entry->cols, 1, hook_cfg(), ws, r.ws_bytes,
                         stream) != Q4RDNA_OK)
         return 0;
     g_op_launches.fetch_add(1, std::memory_order_relaxed);
@@ -347,13 +378,13 @@ int q4rdna_mul_mat_glu(const char *up_name, int64_t up_ne0, int64_t up_ne1, cons
     Registry &r = registry();
     std::lock_guard<std::mutex> lock(r.mu);
     Found up, gate;
-    if (!find(r, up_name, up_ne0, up_ne1, up) || !find(r, gate_name, gate_ne0, gate_ne1, gate)) return 0;
+    if (!find(r, up_name, up_ne0, up_ne1, (cudaStream_t)stream, up) || !find(r, gate_name, gate_ne0, gate_ne1, (cudaStream_t)stream, gate)) return 0;
     if (up.entry->rows != gate.entry->rows || up.entry->cols != gate.entry->cols ||
         x_ne0 != (int64_t)up.entry->cols || y_nelements != (int64_t)up.entry->rows)
         return 0;
     void *ws = stream_workspace(r, (cudaStream_t)stream);
     if (r.ws_bytes && ws == nullptr) return 0;
-    if (q4rdna_gemv_swiglu(up.tiles, gate.tiles, x, y, (int)up.entry->rows, (int)up.entry->cols, 1, nullptr, ws,
+    if (q4rdna_gemv_swiglu(up.tiles, gate.tiles, x, y, (int)up.entry->rows, (int)up.entry->cols, 1, hook_cfg(), ws,
                            r.ws_bytes, stream) != Q4RDNA_OK)
         return 0;
     g_op_launches.fetch_add(1, std::memory_order_relaxed);
@@ -400,6 +431,7 @@ void q4rdna_report_stats(void) {
 }
 
 void q4rdna_registry_reset(void) {
+    noalloc_forget_devices();
     Registry &r = registry();
     std::lock_guard<std::mutex> lock(r.mu);
     for (auto &kv : r.ws) cudaFree(kv.second);

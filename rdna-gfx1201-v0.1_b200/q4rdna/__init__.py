@@ -8,6 +8,9 @@ The operator surface mirrors the reference's ggml hooks
 (source/q4rdna.cuh:5-24): ``mul_mat``, ``mul_mat_add`` and ``mul_mat_glu`` take
 a ggml tensor name plus shapes and return True when the work was enqueued,
 False when the caller must fall back to its stock kernel.
+
+The library is mapped on first use (``q4rdna.lib``, or any call), not at
+import: ``import q4rdna.synth`` or ``q4rdna.format`` alone loads no CUDA code.
 """
 from __future__ import annotations
 
@@ -37,8 +40,11 @@ class Q4RDNAError(RuntimeError):
         super().__init__(f"q4rdna: {STATUS.get(status, status)} ({status_string(status)}){': ' + what if what else ''}")
 
 
+CFG_OVERLAP_PREVIOUS = 1
+
+
 class Cfg(ctypes.Structure):
-    _fields_ = [("split", c_int), ("reserved", c_int * 7)]
+    _fields_ = [("split", c_int), ("flags", c_int), ("reserved", c_int * 6)]
 
 
 class GemvDesc(ctypes.Structure):
@@ -79,6 +85,7 @@ def _bind(lib):
         "q4rdna_plan_set_segments": (c_int, [P, c_int]),
         "q4rdna_plan_set_gather": (c_int, [P, c_int, c_int, P, c_size_t, POINTER(P), POINTER(P), POINTER(P)]),
         "q4rdna_plan_gather_parity": (c_int, [P]),
+        "q4rdna_plan_set_gather_timeout": (c_int, [P, ctypes.c_uint32]),
         "q4rdna_ipc_alloc": (c_int, [c_size_t, POINTER(P), ctypes.c_char_p]),
         "q4rdna_ipc_open": (c_int, [ctypes.c_char_p, POINTER(P)]),
         "q4rdna_ipc_close": (c_int, [P]),
@@ -105,7 +112,24 @@ def _bind(lib):
     return lib
 
 
-lib = _bind(ctypes.CDLL(LIB_PATH)) if os.path.exists(LIB_PATH) else None
+_lib_handle = None
+
+
+def _load_lib():
+    """The bound library, mapped on the first call; None when it was not built."""
+    global _lib_handle
+    if _lib_handle is None and os.path.exists(LIB_PATH):
+        _lib_handle = _bind(ctypes.CDLL(LIB_PATH))
+    return _lib_handle
+
+
+def __getattr__(name):
+    # ``q4rdna.lib``: the ctypes library (None if not built), mapped lazily
+    if name == "lib":
+        return _load_lib()
+    raise AttributeError(f"module 'q4rdna' has no attribute {name!r}")
+
+
 SYMBOLS = [
     "q4rdna_status_string", "q4rdna_version", "q4rdna_select_split", "q4rdna_workspace_bytes",
     "q4rdna_workspace_init", "q4rdna_gemv", "q4rdna_gemv_add", "q4rdna_gemv_swiglu", "q4rdna_dequant_f32", "q4rdna_pack_bf16",
@@ -113,7 +137,8 @@ SYMBOLS = [
     "q4rdna_gemv_noalloc",
     "q4rdna_q4k_bytes", "q4rdna_q4k_gemv", "q4rdna_q4k_dequant_f32",
     "q4rdna_plan_create", "q4rdna_plan_run", "q4rdna_plan_get_info", "q4rdna_plan_destroy",
-    "q4rdna_plan_run_host", "q4rdna_plan_set_segments", "q4rdna_plan_set_gather", "q4rdna_plan_gather_parity", "q4rdna_ipc_alloc", "q4rdna_ipc_open",
+    "q4rdna_plan_run_host", "q4rdna_plan_set_segments", "q4rdna_plan_set_gather", "q4rdna_plan_gather_parity",
+    "q4rdna_plan_set_gather_timeout", "q4rdna_ipc_alloc", "q4rdna_ipc_open",
     "q4rdna_ipc_close", "q4rdna_ipc_free",
     "q4rdna_sidecar_open", "q4rdna_sidecar_close", "q4rdna_sidecar_count", "q4rdna_sidecar_entry",
     "q4rdna_sidecar_find", "q4rdna_mul_mat", "q4rdna_mul_mat_add", "q4rdna_mul_mat_glu",
@@ -122,6 +147,7 @@ SYMBOLS = [
 
 
 def _lib():
+    lib = _load_lib()
     if lib is None:
         raise RuntimeError(f"q4rdna CUDA library not built: {LIB_PATH} is missing (run __graft_entry__.build())")
     return lib
@@ -149,9 +175,10 @@ def take_fault() -> int:
     return int(_lib().q4rdna_take_fault())
 
 
-def _cfg(split: int):
+def _cfg(split: int, flags: int = 0):
     c = Cfg()
     c.split = int(split)
+    c.flags = int(flags)
     return ctypes.byref(c)
 
 
@@ -456,14 +483,7 @@ def report_stats() -> None:
     _lib().q4rdna_report_stats()
 
 
-_KERNELS = {"i8": "q4::q4_gemv_i8_kernel", "i8tma": "q4::q4_gemv_i8_tma_kernel", "ldg": "q4::q4_gemv_kernel"}
-
-
 def kernel_name(B: int = 1) -> str:
-    """Name of the GEMV kernel the library launches for batch B: the int8 tile
-    path for B = 3..16 (the f16 tile path when Q4RDNA_TILE=f16), else the int8
-    tensor-core kernel unless Q4RDNA_KERNEL selects another variant (read by the
-    library at its first launch, same names)."""
-    if B >= int(os.environ.get("Q4RDNA_TILE_MIN_BATCH") or 3):
-        return "q4::q4_gemv_mbh_kernel" if os.environ.get("Q4RDNA_TILE") == "f16" else "q4::q4_gemv_mb_kernel"
-    return _KERNELS.get(os.environ.get("Q4RDNA_KERNEL") or "i8", _KERNELS["i8"])
+    """Name of the GEMV kernel the library launches for batch B: the int8
+    tensor-core batch-1 kernel for B = 1..2, the int8 tile path for B = 3..16."""
+    return "q4::q4_gemv_mb_kernel" if B >= 3 else "q4::q4_gemv_i8_kernel"

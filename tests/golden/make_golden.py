@@ -44,7 +44,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 sys.path.insert(0, os.path.join(REPO, "rdna-gfx1201-v0.1_b200"))
-REF_SRC = "/root/reference/source"
+# The reference checkout: $Q4RDNA_REFERENCE, else the directory "reference"
+# beside this repository.
+REF_SRC = os.path.join(os.environ.get("Q4RDNA_REFERENCE") or os.path.join(os.path.dirname(REPO), "reference"),
+                       "source")
 
 import oracle  # noqa: E402
 from q4rdna import format as fmt, synth  # noqa: E402

@@ -55,8 +55,9 @@ def test_no_alloc_matches_workspace_entry_point_on_two_calls(cuda):
         xd = torch.from_numpy(x).to(cuda)
         y_ref = _with_workspace(td, xd, N, K, B).cpu().numpy()
         y = _no_alloc(td, xd, N, K, B).cpu().numpy()
-        _, mag = oracle.gemv_f64(tiles, x, N, K, threads=8)
-        tolerance.check(y, y_ref.astype(np.float64), mag, f"no-alloc vs workspace {N}x{K} B={B}")
+        y64, mag = oracle.gemv_f64(tiles, x, N, K, threads=8)
+        tolerance.check(y, y64, mag, f"no-alloc vs fp64 oracle {N}x{K} B={B}")
+        # and bit for bit what the workspace entry point computes with the same split
         assert np.array_equal(y.view(np.uint32), y_ref.view(np.uint32))
 
 
