@@ -478,7 +478,7 @@ QKV = (".attn_q.", ".attn_k.", ".attn_v.")
 
 
 def build_step(model: str, rank: int, world: int, device, seed: int, layers: int = 0, B: int = 1,
-               norm: bool = False, hybrid: bool = False):
+               norm: bool = False, hybrid: bool = False, split: int = 0):
     """Weights (this rank's row shard of every tensor), activations and outputs
     of one decode step, laid out by q4rdna.tp.Layout so that a step's inputs and
     outputs are each one contiguous buffer (one copy each way for the
@@ -517,6 +517,8 @@ def build_step(model: str, rank: int, world: int, device, seed: int, layers: int
             t = synth.tiles_torch(s.rows, s.K, seed + 1 + i * world + rank, device)
             tb = s.rows * s.K * 34 // 64
         d = {"tiles": t, "x": x_all[B * xo:B * (xo + s.K)].view(B, s.K), "y": lay.local_view(y_all, i)}
+        if split:
+            d["split"] = split
         if q4k:
             d["format"] = q4rdna.FORMAT_Q4K
         if norm:  # x is the raw hidden state; the plan normalises it on the fly
@@ -613,6 +615,92 @@ def time_drop_in_step(descs, B: int, steps: int, abytes: int, overlap: bool = Fa
             "frac": round(gbs / peak, 4)}
 
 
+LAYER_STAGES = (("attn_q", "attn_k", "attn_v"), ("attn_output",), ("ffn_gate", "ffn_up"), ("ffn_down",))
+
+
+def time_layered(args, descs, names, world, rank, B, p2p, steps, dev):
+    """The step as a decoder runs it under tensor parallelism: per layer four
+    dependent stages (q/k/v, o, gate/up, down), each one plan followed by its
+    all-gather (fused into the plan with p2p, else one NCCL all-gather), in
+    stream order.  The weights and activations are the step's; every stage has
+    its own output and gathered buffers.  p2p: all stages' plans run through
+    one q4rdna_plan_run_many call per step; NCCL: the stages are captured once
+    in a CUDA graph.  Device time per step, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    import q4rdna
+    from q4rdna import tp
+
+    by_name = {n[0]: i for i, n in enumerate(names)}
+    nlayers = len({n[0].split(".")[1] for n in names})
+    plans, gathers, keep = [], [], []
+    for L in range(nlayers):
+        for stage in LAYER_STAGES:
+            idx = [by_name[f"blk.{L}.{t}.weight"] for t in stage]
+            lay = tp.Layout([names[i] for i in idx], world, B=B)
+            y = torch.zeros(B * lay.ysz, dtype=torch.float32, device=dev)
+            sd = [{"tiles": descs[i]["tiles"], "x": descs[i]["x"], "y": lay.local_view(y, k)} for k, i in enumerate(idx)]
+            plan = q4rdna.Plan(sd, B=B)
+            g = None
+            if world > 1:
+                g = tp.PeerGather(plan, lay, y) if p2p else torch.empty(world * y.numel(), device=dev)
+            plans.append(plan)
+            gathers.append(g)
+            keep.append((sd, y))
+    stream = torch.cuda.current_stream()
+    graph = None
+    if world > 1 and not p2p:
+        cap = torch.cuda.Stream()
+
+        def once():
+            for plan, g, (_, y) in zip(plans, gathers, keep):
+                plan.run()
+                tp.all_gather(y, g)
+
+        with torch.cuda.stream(cap):
+            once()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=cap):
+            once()
+
+    def step():
+        if graph is not None:
+            graph.replay()
+        else:
+            q4rdna.run_plans(plans, stream)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    fault = q4rdna.take_fault()
+    del graph
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    for plan, g in zip(plans, gathers):
+        if isinstance(g, tp.PeerGather):
+            g.close()
+        plan.close()
+    return {"how": f"{len(plans)} dependent plans per step ({len(LAYER_STAGES)} stages per layer), each followed by "
+                   + ("its all-gather fused into the plan (P2P stores + flag exchange), one q4rdna_plan_run_many call"
+                      if p2p else "one NCCL all-gather, captured in one CUDA graph") if world > 1 else
+                   f"{len(plans)} dependent plans per step ({len(LAYER_STAGES)} stages per layer), no gather (one GPU)",
+            "plans": len(plans), "us_per_step": round(t.item() * 1e3, 2), "fault_flags": fault}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -637,8 +725,12 @@ def run_ours(args):
     B = args.batch
     if args.hybrid and args.norm:
         raise SystemExit("--hybrid takes no --norm (the Q4_K kernel has no fused RMSNorm)")
+    emulate = args.emulate_world if world == 1 and args.emulate_world > 1 else 0
+    if args.tp_layered and (args.hybrid or args.norm):
+        raise SystemExit("--tp-layered runs the plain Q4_RDNA step (no --hybrid, no --norm)")
     descs, x_all, y_all, wbytes, abytes, ntensors, lay, nweights = build_step(
-        args.model, rank, world, dev, args.seed, args.layers, B, args.norm, args.hybrid)
+        args.model, rank if not emulate else 0, world if not emulate else emulate, dev, args.seed, args.layers, B,
+        args.norm, args.hybrid, args.plan_split)
     plan = q4rdna.Plan(descs, B=B)
     plan.set_segments(args.run_segments)
     info = plan.info()
@@ -683,6 +775,30 @@ def run_ours(args):
     launches = q4rdna.launch_count() - l0
     ms_total = t0.elapsed_time(t1)
     kern_ms = statistics.mean(a.elapsed_time(b) for a, b in k_ev)
+    per_rank = None
+    if world > 1:
+        # the same plan without its gather on every rank: the plan kernel's own
+        # time, and how far apart the ranks finish it (arrival skew)
+        alone = q4rdna.Plan(descs, B=B)
+        for _ in range(3):
+            alone.run(stream)
+        barrier()
+        a_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for i in range(args.steps):
+            a_ev[i][0].record(stream)
+            alone.run(stream)
+            a_ev[i][1].record(stream)
+        barrier()
+        alone_ms = statistics.mean(a.elapsed_time(b) for a, b in a_ev)
+        alone.close()
+        mine = torch.tensor([alone_ms, kern_ms], dtype=torch.float64, device=dev)
+        allr = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(allr, mine)
+        pa = [round(v[0].item() * 1e3, 2) for v in allr]
+        pw = [round(v[1].item() * 1e3, 2) for v in allr]
+        per_rank = {"plan_alone_us": pa, ("plan_with_gather_us" if p2p else "plan_us_before_nccl"): pw,
+                    "plan_alone_skew_us": round(max(pa) - min(pa), 2),
+                    "gather_cost_us": round(max(pw) - max(pa), 2) if p2p else None}
     q4k_leg = None
     if args.hybrid:
         # the Q4_K tensors alone, as one plan: the Q4_K kernel's own roofline
@@ -715,19 +831,29 @@ def run_ours(args):
         if B <= 2:
             drop_in["overlapped"] = time_drop_in_step(descs, B, args.steps, abytes, overlap=True)
 
-    # end-to-end: pinned host activations in, outputs out, every step
+    layered = None
+    if args.tp_layered:
+        names = [(s_.name, s_.N, s_.K) for s_ in lay.slots]
+        layered = time_layered(args, descs, names, world, rank, B, p2p, args.steps, dev)
+        layered["gbs"] = round(abytes * world / (layered["us_per_step"] * 1e-6) / 1e9, 1)
+
+    # end-to-end: pinned host activations in, outputs out, every step.  Every
+    # rank copies in the whole (replicated) activation and brings out its own
+    # outputs: together the ranks' host buffers hold the whole step's result.
     x_host = torch.empty(x_all.numel(), dtype=torch.float32, pin_memory=True)
     x_host.copy_(x_all)
-    y_host = torch.empty(y_all.numel() * world, dtype=torch.float32, pin_memory=True)
+    y_host = torch.empty(y_all.numel(), dtype=torch.float32, pin_memory=True)
 
     def e2e_step():
-        if world == 1:
-            # the public host-buffer entry point: copies overlapped with the GEMVs
+        if world == 1 or p2p:
+            # the public host-buffer entry point: input copies overlapped with the
+            # GEMVs, outputs stored straight into the host buffer (with p2p also
+            # into every rank's gathered buffer, then the flag exchange)
             plan.run_host(x_host, x_all, y_all, y_host, segments=args.segments, stream=stream)
             return
         x_all.copy_(x_host, non_blocking=True)
-        out_dev = step()
-        y_host.copy_(out_dev, non_blocking=True)
+        step()
+        y_host.copy_(y_all, non_blocking=True)
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
@@ -763,11 +889,15 @@ def run_ours(args):
             "data": "synthetic: uniform int4 codes, fp16 scales |N(0,1)|*0.003, x ~ N(0,1) f32 (no Qwen3 weights offline)"
                     + ("; Q4_K tensors: uniform quant and 6-bit scale bytes, d and dmin fp16((0.5+|N(0,1)|)*2e-4)"
                        if args.hybrid else ""),
-            "config": step_config(args, world, p2p),
-            "plan": {"items": info["items"], "grid": info["grid"]},
+            "config": step_config(args, world, p2p) if not emulate else
+                      {**step_config(args, 1, False), "emulated": f"rank 0 of {emulate}: its row shard of every tensor, "
+                                                                  "no gather, on one GPU",
+                       "algo_bytes_per_step": abytes, "weight_bytes_per_step": wbytes},
+            "plan": {"items": info["items"], "grid": info["grid"], "split": args.plan_split or "plan-wide choice"},
             "e2e": {"value": round(total_algo / (e2e_ms / args.steps * 1e-3) / 1e9, 2), "unit": UNIT,
                     "us_per_step": round(e2e_ms / args.steps * 1e3, 2),
-                    "h2d_bytes_per_step": x_all.numel() * 4, "d2h_bytes_per_step": y_host.numel() * 4},
+                    "h2d_bytes_per_step": x_all.numel() * 4 * world, "d2h_bytes_per_step": y_host.numel() * 4 * world,
+                    **({"per_rank": "each rank: the whole activation in, its own outputs out"} if world > 1 else {})},
             "roofline": {"bound": "hbm", "kernel": q4rdna.kernel_name(B) + (" + q4k::q4k_gemv_kernel" if args.hybrid else "")
                          + (" (plan + fused gather)" if p2p else " (plan)"), "achieved": round(achieved, 1),
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
@@ -776,6 +906,8 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "gpu_launches": launches,
             **({"drop_in_step": drop_in} if drop_in else {}),
+            **({"per_rank": per_rank} if per_rank else {}),
+            **({"layered": layered} if layered else {}),
             **({"q4k": q4k_leg} if q4k_leg else {}),
             "clocks": clk.summary(),
         }
@@ -859,6 +991,12 @@ def main():
     ap.add_argument("--single-no-hook", action="store_true", help="--single: skip the name-keyed hook leg")
     ap.add_argument("--single-ncu", action="store_true",
                     help="--single: only 3 eager calls per shape at the selector's split (for an ncu launch list)")
+    ap.add_argument("--plan-split", type=int, default=0,
+                    help="force this split-K factor on every tensor of the step's plan (0: the plan-wide choice)")
+    ap.add_argument("--emulate-world", type=int, default=0,
+                    help="N = 1 only: run rank 0's row shards of a W-way split (no gather), e.g. for ncu")
+    ap.add_argument("--tp-layered", action="store_true",
+                    help="also time the step as 4 dependent plans per layer, each followed by its all-gather")
     ap.add_argument("--layers", type=int, default=0,
                     help="only the first L layers (small cases for profiling); 0 = the whole model")
     args = ap.parse_args()

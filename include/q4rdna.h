@@ -240,12 +240,22 @@ void q4rdna_plan_destroy(q4rdna_plan *plan);
  * The first call with a given set of buffers does the capture; make it outside
  * any stream capture of the caller.  The
  * segments' activation ranges must not overlap, nor their output ranges.
+ * With a fused gather (q4rdna_plan_set_gather) the segments also store into
+ * every rank's gathered buffer and the run ends with the flag exchange; y_host
+ * then receives this rank's outputs (its y buffer), and the calls are direct
+ * launches (no graph).
  * Ordered after prior work on `stream`; `stream` waits for the last copy.  No
  * synchronisation; calls on one plan must not overlap.  No reference
  * counterpart (the reference keeps activations on the GPU). */
 q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *x_dev, size_t x_bytes,
                                    const void *y_dev, void *y_host, size_t y_bytes, int segments,
                                    q4rdna_stream_t stream);
+
+/* Runs plans[0], plans[1], ... in order on `stream`, each exactly as
+ * q4rdna_plan_run does (with its fused gather, if set): one host call for a
+ * sequence of dependent plans, e.g. a decoder layer's stages under tensor
+ * parallelism.  Stops at the first failing plan and returns its status. */
+q4rdna_status q4rdna_plan_run_many(q4rdna_plan *const *plans, int count, q4rdna_stream_t stream);
 
 /* How q4rdna_plan_run executes the plan: as `segments` launches of consecutive
  * descriptors (about equal weight bytes) that alternate between two library

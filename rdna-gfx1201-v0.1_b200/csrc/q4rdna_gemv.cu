@@ -45,7 +45,8 @@ namespace q4 {
 constexpr int kWarps = 8;             // warps per CTA
 constexpr int kThreads = kWarps * 32;
 
-constexpr int kMaxMirrors = 8;  // GPUs of one box
+constexpr int kMaxWorld = 8;    // GPUs of one box
+constexpr int kMaxMirrors = kMaxWorld + 1;  // every rank's gathered buffer + a host-mapped output (run_host)
 
 struct Task {
     const uint8_t *w;   // primary tiles (W, or W_up for SwiGLU)
@@ -233,6 +234,7 @@ KernelCfg kernel_cfg(int pb, bool dual = true, bool norm = false) {
     return dual ? i8_cfg_n<true, false>(pb) : i8_cfg_n<false, false>(pb);
 }
 
+// dual: the launch holds a SwiGLU task
 const void *cta_kernel(int pb, bool dual) {
     if (pb <= 1) return dual ? (const void *)q4_gemv_cta_kernel<1, true> : (const void *)q4_gemv_cta_kernel<1, false>;
     return dual ? (const void *)q4_gemv_cta_kernel<2, true> : (const void *)q4_gemv_cta_kernel<2, false>;
@@ -404,6 +406,28 @@ q4rdna_status launch(const Launch &L, int grid, int pb, bool dual, cudaStream_t 
     return Q4RDNA_OK;
 }
 
+// The CTA-split kernel (q4rdna_gemv_cta.cuh, B = 1..2): one CTA per item of
+// L (total_items CTAs); overlap: programmatic dependent launch.
+q4rdna_status launch_cta(const Launch &L, int pb, bool dual, cudaStream_t stream, bool overlap = false) {
+    Launch arg = L;
+    void *args[] = {&arg};
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)L.total_items);
+    lc.blockDim = dim3(kThreads);
+    lc.stream = stream;
+    cudaLaunchAttribute at[1];
+    if (overlap) {
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        lc.attrs = at;
+        lc.numAttrs = 1;
+    }
+    if (cudaLaunchKernelExC(&lc, cta_kernel(pb, dual), args) != cudaSuccess) return Q4RDNA_ERR_CUDA;
+    if (cudaGetLastError() != cudaSuccess) return Q4RDNA_ERR_CUDA;
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return Q4RDNA_OK;
+}
+
 q4rdna_status gemv_common(int op, const uint8_t *w, const uint8_t *w2, const float *x, const float *add, float *y,
                           int N, int K, int B, const q4rdna_cfg *cfg, void *ws, size_t ws_bytes,
                           cudaStream_t stream, const float *gn = nullptr, float eps = 0.0f) {
@@ -450,30 +474,8 @@ q4rdna_status gemv_common(int op, const uint8_t *w, const uint8_t *w2, const flo
     T.nss = (gn != nullptr && sp.S > 1) ? part + partial_bytes(N, B, sp.S, op) / sizeof(float) : nullptr;
     L.total_items = (long long)RB * sp.S;
     const bool dual = op == Q4RDNA_OP_SWIGLU;
-    if (B < kTileMinBatch && gn == nullptr) {
-        // single call at B = 1..2: one CTA per (row block, K-range), K-range
-        // split over the CTA's warps (q4rdna_gemv_cta.cuh)
-        CtaArgs a;
-        a.T = T;
-        a.B = B;
-        a.Gw = (sp.Gs + kWarps - 1) / kWarps;
-        void *args[] = {&a};
-        cudaLaunchConfig_t lc = {};
-        lc.gridDim = dim3((unsigned)(RB * sp.S));
-        lc.blockDim = dim3(kThreads);
-        lc.stream = stream;
-        cudaLaunchAttribute at[1];
-        if (cfg != nullptr && (cfg->flags & Q4RDNA_CFG_OVERLAP_PREVIOUS)) {
-            at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-            at[0].val.programmaticStreamSerializationAllowed = 1;
-            lc.attrs = at;
-            lc.numAttrs = 1;
-        }
-        if (cudaLaunchKernelExC(&lc, cta_kernel(B, dual), args) != cudaSuccess) return Q4RDNA_ERR_CUDA;
-        if (cudaGetLastError() != cudaSuccess) return Q4RDNA_ERR_CUDA;
-        g_launches.fetch_add(1, std::memory_order_relaxed);
-        return Q4RDNA_OK;
-    }
+    if (B < kTileMinBatch && gn == nullptr)  // one CTA per (row block, K-range) (q4rdna_gemv_cta.cuh)
+        return launch_cta(L, B, dual, stream, cfg != nullptr && (cfg->flags & Q4RDNA_CFG_OVERLAP_PREVIOUS));
     return launch(L, grid_for(L.total_items, B, dual, d), B, dual, stream, gn != nullptr);
 }
 
@@ -485,7 +487,7 @@ using namespace q4;
 // order), lane p raises this rank's flag at rank p, then waits, bounded, for
 // rank p's flag of this epoch here.
 struct GatherSignal {
-    uint32_t *peer[kMaxMirrors];  // every rank's flag array, as mapped in this process
+    uint32_t *peer[kMaxWorld];    // every rank's flag array, as mapped in this process
     uint32_t *local;              // this rank's flag array
     int world, rank;
     uint32_t epoch;
@@ -608,6 +610,7 @@ struct q4rdna_plan {
     int count = 0, B = 1, nb = 1, grid = 1;
     bool dual = false;  // the plan holds a SwiGLU task
     bool norm = false;  // the plan holds a fused-RMSNorm task
+    bool cta = false;   // runs on the CTA-split kernel (one CTA per item), else the persistent warp-item kernel
     long long items = 0;
     Task *table = nullptr;     // device
     void *workspace = nullptr; // device
@@ -657,6 +660,12 @@ struct q4rdna_plan {
 };
 
 namespace {
+// One launch of (a segment of) a plan on its kernel.
+q4rdna_status plan_launch(const q4rdna_plan *plan, const Launch &L, int grid, cudaStream_t stream) {
+    if (plan->cta) return launch_cta(L, plan->nb, plan->dual, stream);
+    return launch(L, grid, plan->nb, plan->dual, stream, plan->norm);
+}
+
 q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t xb, const uint8_t *yd,
                              size_t yb, bool graded = false, const uint8_t *yh = nullptr);
 q4rdna_status launch_segments(q4rdna_plan *plan, cudaStream_t cs, const uint8_t *xh, uint8_t *xd, const uint8_t *yd,
@@ -770,6 +779,16 @@ q4rdna_status plan_create_rdna(const q4rdna_gemv_desc *descs, int count, int B, 
     const long long workers = resident_workers(B, any_dual_task, d);
     const double want_items = kPlanItemsPerWorker * (double)workers;
     const int plan_split = total_rb > 0 ? (int)std::max(1.0, std::ceil(want_items / (double)total_rb)) : 1;
+    // Plans too small for unsplit warp items (plan_split > 1: a tensor-parallel
+    // rank's shards, a decoder stage) run on the CTA-split kernel at B = 1..2
+    // (no fused norm): a CTA per (row block, K-range) with the K-range split
+    // again over its 8 warps, and as many K-ranges per tensor as fit one wave
+    // of resident CTAs (at least one group per warp).
+    bool any_norm_task = false;
+    for (int i = 0; i < count; ++i) any_norm_task = any_norm_task || descs[i].norm_weight != nullptr;
+    const bool cta = B < kTileMinBatch && !any_norm_task && plan_split > 1;
+    const long long ctas = (long long)d.sms * d.occ_cta[std::min(B, 2) - 1][any_dual_task];
+    const int cta_split = total_rb > 0 ? (int)std::max<long long>(1, ctas / total_rb) : 1;
     for (int i = 0; i < count; ++i) {
         const q4rdna_gemv_desc &e = descs[i];
         q4rdna_status st = check_shape(e.N, e.K, B);
@@ -784,7 +803,7 @@ q4rdna_status plan_create_rdna(const q4rdna_gemv_desc *descs, int count, int B, 
         const int planes = e.op == Q4RDNA_OP_SWIGLU ? 2 : 1;
         const int G = e.K / Q4_GROUP;
         const int RB = (e.N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
-        const int req = e.split > 0 ? e.split : std::min(plan_split, G);
+        const int req = e.split > 0 ? e.split : cta ? std::min(cta_split, std::max(1, G / kWarps)) : std::min(plan_split, G);
         const Split sp = make_split(G, req);
         Task &T = host[i];
         T.w = e.tiles; T.w2 = e.gate_tiles; T.x = e.x; T.add = e.add; T.y = e.y;
@@ -825,7 +844,8 @@ q4rdna_status plan_create_rdna(const q4rdna_gemv_desc *descs, int count, int B, 
     p->count = count; p->B = B; p->nb = B; p->items = items; p->dual = any_dual;
     for (int i = 0; i < count; ++i) p->norm = p->norm || descs[i].norm_weight != nullptr;
     p->host = host;
-    p->grid = grid_for(items, B, any_dual, d);
+    p->cta = cta;
+    p->grid = cta ? (int)std::min<long long>(items, INT32_MAX) : grid_for(items, B, any_dual, d);
     p->ws_bytes = ws_total; p->weight_bytes = wbytes; p->algo_bytes = abytes;
     *out = p;
     return Q4RDNA_OK;
@@ -892,6 +912,20 @@ q4rdna_status launch_q4k(q4rdna_plan *plan, cudaStream_t stream) {
 }
 }  // namespace
 
+// The flag exchange that closes run `epoch` of a gather plan (after its GEMV
+// launches, in stream order).
+static q4rdna_status launch_signal(q4rdna_plan *plan, uint32_t epoch, cudaStream_t stream) {
+    GatherSignal sg = plan->sig;
+    sg.epoch = epoch;
+    void *args[] = {&sg};
+    if (cudaLaunchKernel((const void *)q4_gather_signal_kernel, dim3(1), dim3(32), args, 0, stream) != cudaSuccess)
+        return Q4RDNA_ERR_CUDA;
+    if (cudaGetLastError() != cudaSuccess) return Q4RDNA_ERR_CUDA;
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    plan->epoch = epoch;
+    return Q4RDNA_OK;
+}
+
 q4rdna_status q4rdna_plan_run(q4rdna_plan *plan, q4rdna_stream_t stream) {
     if (plan == nullptr) return Q4RDNA_ERR_INVALID_ARGUMENT;
     int dev = -1;
@@ -915,7 +949,7 @@ q4rdna_status q4rdna_plan_run(q4rdna_plan *plan, q4rdna_stream_t stream) {
             L.ntasks = plan->count;
             L.B = plan->B;
             L.total_items = plan->items;
-            st = launch(L, plan->grid, plan->nb, plan->dual, (cudaStream_t)stream, plan->norm);
+            st = plan_launch(plan, L, plan->grid, (cudaStream_t)stream);
         }
         if (st != Q4RDNA_OK) return st;
         return launch_q4k(plan, (cudaStream_t)stream);
@@ -930,19 +964,10 @@ q4rdna_status q4rdna_plan_run(q4rdna_plan *plan, q4rdna_stream_t stream) {
         L.ntasks = plan->count;
         L.B = plan->B;
         L.total_items = plan->items;
-        st = launch(L, plan->grid, plan->nb, plan->dual, (cudaStream_t)stream, plan->norm);
+        st = plan_launch(plan, L, plan->grid, (cudaStream_t)stream);
     }
     if (st != Q4RDNA_OK) return st;
-    GatherSignal sg = plan->sig;
-    sg.epoch = epoch;
-    void *args[] = {&sg};
-    if (cudaLaunchKernel((const void *)q4_gather_signal_kernel, dim3(1), dim3(32), args, 0, (cudaStream_t)stream) !=
-        cudaSuccess)
-        return Q4RDNA_ERR_CUDA;
-    if (cudaGetLastError() != cudaSuccess) return Q4RDNA_ERR_CUDA;
-    g_launches.fetch_add(1, std::memory_order_relaxed);
-    plan->epoch = epoch;
-    return Q4RDNA_OK;
+    return launch_signal(plan, epoch, (cudaStream_t)stream);
 }
 
 q4rdna_status q4rdna_plan_set_gather(q4rdna_plan *plan, int world, int rank, const float *y_base,
@@ -950,7 +975,7 @@ q4rdna_status q4rdna_plan_set_gather(q4rdna_plan *plan, int world, int rank, con
                                      uint32_t *const *flags) {
     if (plan == nullptr || y_base == nullptr || gathered0 == nullptr || gathered1 == nullptr || flags == nullptr)
         return Q4RDNA_ERR_INVALID_ARGUMENT;
-    if (world < 2 || world > kMaxMirrors || rank < 0 || rank >= world || plan->gather)
+    if (world < 2 || world > kMaxWorld || rank < 0 || rank >= world || plan->gather)
         return Q4RDNA_ERR_INVALID_ARGUMENT;
     if (!plan->q4k_host.empty() || plan->count == 0) return Q4RDNA_ERR_UNSUPPORTED;
     int dev = -1;
@@ -1079,6 +1104,13 @@ q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t
             return Q4RDNA_ERR_CUDA;
         for (int par = 0; p->gather && par < 2; ++par) {
             std::vector<Task> gt(p->ghost[par].begin() + first, p->ghost[par].begin() + last);
+            if (direct)  // the gather's mirrors, then the host-mapped output
+                for (size_t k = 0; k < gt.size(); ++k) {
+                    const Task &T = p->host[first + k];
+                    gt[k].mirror[gt[k].nmirror] =
+                        reinterpret_cast<float *>(yh_dev + (reinterpret_cast<const uint8_t *>(T.y) - yd));
+                    gt[k].nmirror += 1;
+                }
             if ((g.gtable[par] = upload_tasks(gt)) == nullptr) return Q4RDNA_ERR_CUDA;
         }
         first = last;
@@ -1148,7 +1180,7 @@ q4rdna_status launch_segments(q4rdna_plan *plan, cudaStream_t cs, const uint8_t 
         L.ntasks = sg.count;
         L.B = plan->B;
         L.total_items = sg.items;
-        const q4rdna_status st = launch(L, sg.grid, plan->nb, plan->dual, c, plan->norm);
+        const q4rdna_status st = plan_launch(plan, L, sg.grid, c);
         if (st != Q4RDNA_OK) return st;
         if (cudaEventRecord(sg.y_ready, c) != cudaSuccess) return Q4RDNA_ERR_CUDA;
         if (!out_copies) continue;
@@ -1179,7 +1211,6 @@ q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *
     if (plan == nullptr || x_host == nullptr || x_dev == nullptr || y_dev == nullptr || y_host == nullptr ||
         segments < 0)
         return Q4RDNA_ERR_INVALID_ARGUMENT;
-    if (plan->gather) return Q4RDNA_ERR_UNSUPPORTED;
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev != plan->device) return Q4RDNA_ERR_DEVICE;
     if (!plan->q4k_host.empty()) {
@@ -1204,6 +1235,17 @@ q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *
     } else {
         for (const auto &sg : plan->segs)
             if (sg.x_hi > x_bytes || sg.y_hi > y_bytes) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    }
+    if (plan->gather) {
+        // a gather plan: the segments store into every rank's gathered buffer
+        // (and the host buffer when it is mapped), then the flag exchange; the
+        // run's epoch changes per call, so these are direct launches
+        const uint32_t epoch = plan->epoch + 1;
+        const q4rdna_status st = launch_segments(plan, (cudaStream_t)stream, static_cast<const uint8_t *>(x_host),
+                                                 static_cast<uint8_t *>(x_dev), static_cast<const uint8_t *>(y_dev),
+                                                 static_cast<uint8_t *>(y_host), (int)(epoch & 1));
+        if (st != Q4RDNA_OK) return st;
+        return launch_signal(plan, epoch, (cudaStream_t)stream);
     }
     if (!host_graph()) {
         return launch_segments(plan, (cudaStream_t)stream, static_cast<const uint8_t *>(x_host),
@@ -1244,6 +1286,15 @@ q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *
     }
     if (cudaGraphLaunch(hg.exec, (cudaStream_t)stream) != cudaSuccess) return Q4RDNA_ERR_CUDA;
     g_launches.fetch_add(hg.launches, std::memory_order_relaxed);
+    return Q4RDNA_OK;
+}
+
+q4rdna_status q4rdna_plan_run_many(q4rdna_plan *const *plans, int count, q4rdna_stream_t stream) {
+    if (plans == nullptr || count < 0) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    for (int i = 0; i < count; ++i) {
+        const q4rdna_status st = q4rdna_plan_run(plans[i], stream);
+        if (st != Q4RDNA_OK) return st;
+    }
     return Q4RDNA_OK;
 }
 

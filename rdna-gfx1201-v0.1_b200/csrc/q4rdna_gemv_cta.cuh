@@ -1,5 +1,6 @@
-// Single-call GEMV for B = 1..2 (included into q4rdna_gemv.cu inside namespace
-// q4, after q4rdna_gemv_i8.cuh).
+// CTA-split GEMV for B = 1..2 (included into q4rdna_gemv.cu inside namespace
+// q4, after q4rdna_gemv_i8.cuh): single calls, and plans whose row blocks are
+// too few to give every resident warp a whole-K item.
 //
 // A lone GEMV has too few rows to keep every warp busy with whole-K items: a
 // warp streams one group (4.3 KB) per DRAM round trip, so an item of 64 groups
@@ -23,11 +24,8 @@
 // before any read of x, the workspace or add and any store.  Launched without
 // the attribute, both instructions do nothing.
 
-struct CtaArgs {
-    Task T;  // T.S = CTA K-ranges, T.Gs = groups per K-range
-    int B;
-    int Gw;  // groups per warp
-};
+// The launch is the plans' Launch: one task (single call) or a task table; an
+// item is one CTA, item_begin counts CTA items (RB * S per task).
 
 template <int BB>
 __device__ __forceinline__ void cta_fetch_x(const Task &T, int B, int g, int lane, float2 (&xv)[BB]) {
@@ -37,21 +35,23 @@ __device__ __forceinline__ void cta_fetch_x(const Task &T, int B, int g, int lan
                       : make_float2(0.0f, 0.0f);
 }
 
+template <int BB>
+struct CtaSmem {
+    I8X<BB> xs[kWarps][2];
+    float red[kWarps][2][4][BB][32];  // [warp][plane][q][b][lane]
+    unsigned last;
+};
+
+// One CTA item of task T: row block rb, K-range sc.
 template <int BB, bool DUAL>
-__global__ void __launch_bounds__(kThreads, 2) q4_gemv_cta_kernel(const __grid_constant__ CtaArgs A) {
+__device__ __forceinline__ void cta_item(const Task &T, int B, int rb, int sc, CtaSmem<BB> &sm) {
     constexpr int planes = DUAL ? 2 : 1;
-    __shared__ I8X<BB> xsm[kWarps][2];
-    __shared__ float red[kWarps][planes][4][BB][32];
-    __shared__ unsigned last;
-    const Task &T = A.T;
-    const int B = A.B;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int rb = blockIdx.x / T.S, sc = blockIdx.x % T.S;
+    const int Gw = (T.Gs + kWarps - 1) / kWarps;
     const int gc1 = min((sc + 1) * T.Gs, T.G);
-    const int g0 = sc * T.Gs + warp * A.Gw;
-    const int ng = max(0, min(A.Gw, gc1 - g0));
+    const int g0 = sc * T.Gs + warp * Gw;
+    const int ng = max(0, min(Gw, gc1 - g0));
     const int grp = lane >> 2, c = lane & 3, t = grp >> 1, h = grp & 1;
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     float acc[2][4][BB];
 #pragma unroll
@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(kThreads, 2) q4_gemv_cta_kernel(const __grid_c
             const int tt = DUAL ? (st & 1) : 0, gl = DUAL ? (st >> 1) : st;
             return (tt ? base1 : base0) + (size_t)gl * Q4_TILE_BYTES;
         };
-        I8X<BB>(&xs)[2] = xsm[warp];
+        I8X<BB>(&xs)[2] = sm.xs[warp];
         StepBufI8 buf;
         load_step_i8(buf, base0, c, h);  // weights: not written by the previous kernels
         asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(kThreads, 2) q4_gemv_cta_kernel(const __grid_c
 #pragma unroll
         for (int q = 0; q < 4; ++q)
 #pragma unroll
-            for (int b = 0; b < BB; ++b) red[warp][pl][q][b][lane] = acc[pl][q][b];
+            for (int b = 0; b < BB; ++b) sm.red[warp][pl][q][b][lane] = acc[pl][q][b];
     __syncthreads();
 
     // thread -> outputs (q, b, ln) of the block: row = tile (ln >> 3) of the
@@ -143,12 +143,12 @@ __global__ void __launch_bounds__(kThreads, 2) q4_gemv_cta_kernel(const __grid_c
         for (int pl = 0; pl < planes; ++pl) {
             float s = 0.0f;
 #pragma unroll
-            for (int w = 0; w < kWarps; ++w) s += red[w][pl][q][b][ln];
+            for (int w = 0; w < kWarps; ++w) s += sm.red[w][pl][q][b][ln];
             v[pl] = s;
         }
         const size_t idx = (size_t)b * T.N + row;
         if (T.S == 1) {
-            T.y[idx] = finish(v[0], v[planes - 1], T.op, T.add, idx);
+            put_y(T, idx, finish(v[0], v[planes - 1], T.op, T.add, idx));
         } else {
 #pragma unroll
             for (int pl = 0; pl < planes; ++pl) __stcg(&T.part[(size_t)sc * split_stride + (size_t)pl * B * T.N + idx], v[pl]);
@@ -159,9 +159,9 @@ __global__ void __launch_bounds__(kThreads, 2) q4_gemv_cta_kernel(const __grid_c
     // K-ranges of several CTAs: the last one to arrive adds them in order
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) last = atomicAdd(&T.ticket[rb], 1u) == (unsigned)(T.S - 1) ? 1u : 0u;
+    if (threadIdx.x == 0) sm.last = atomicAdd(&T.ticket[rb], 1u) == (unsigned)(T.S - 1) ? 1u : 0u;
     __syncthreads();
-    if (last == 0) return;
+    if (sm.last == 0) return;
     __threadfence();
     for (int o = threadIdx.x; o < Q4_BLOCK_ROWS * BB; o += kThreads) {
         const int r = o % Q4_BLOCK_ROWS, b = o / Q4_BLOCK_ROWS;
@@ -175,7 +175,23 @@ __global__ void __launch_bounds__(kThreads, 2) q4_gemv_cta_kernel(const __grid_c
             for (int sp = 0; sp < T.S; ++sp) s += __ldcg(&T.part[(size_t)sp * split_stride + (size_t)pl * B * T.N + idx]);
             v[pl] = s;
         }
-        T.y[idx] = finish(v[0], v[planes - 1], T.op, T.add, idx);
+        put_y(T, idx, finish(v[0], v[planes - 1], T.op, T.add, idx));
     }
     if (threadIdx.x == 0) atomicExch(&T.ticket[rb], 0u);
+}
+
+// One CTA per item (not persistent).  HAS_DUAL = false: the launch holds no
+// SwiGLU task, so that path is compiled out.
+template <int BB, bool HAS_DUAL>
+__global__ void __launch_bounds__(kThreads, 2) q4_gemv_cta_kernel(const __grid_constant__ Launch L) {
+    __shared__ CtaSmem<BB> sm;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const long long it = blockIdx.x;
+    const Task &T = find_task(L, it);
+    const int local = (int)(it - T.item_begin);
+    const int rb = local / T.S, sc = local % T.S;
+    if (HAS_DUAL && T.op == Q4RDNA_OP_SWIGLU)
+        cta_item<BB, true>(T, L.B, rb, sc, sm);
+    else
+        cta_item<BB, false>(T, L.B, rb, sc, sm);
 }

@@ -83,6 +83,7 @@ def _bind(lib):
         "q4rdna_plan_destroy": (None, [P]),
         "q4rdna_plan_run_host": (c_int, [P, P, P, c_size_t, P, P, c_size_t, c_int, P]),
         "q4rdna_plan_set_segments": (c_int, [P, c_int]),
+        "q4rdna_plan_run_many": (c_int, [POINTER(P), c_int, P]),
         "q4rdna_plan_set_gather": (c_int, [P, c_int, c_int, P, c_size_t, POINTER(P), POINTER(P), POINTER(P)]),
         "q4rdna_plan_gather_parity": (c_int, [P]),
         "q4rdna_plan_set_gather_timeout": (c_int, [P, ctypes.c_uint32]),
@@ -137,7 +138,7 @@ SYMBOLS = [
     "q4rdna_gemv_noalloc",
     "q4rdna_q4k_bytes", "q4rdna_q4k_gemv", "q4rdna_q4k_dequant_f32",
     "q4rdna_plan_create", "q4rdna_plan_run", "q4rdna_plan_get_info", "q4rdna_plan_destroy",
-    "q4rdna_plan_run_host", "q4rdna_plan_set_segments", "q4rdna_plan_set_gather", "q4rdna_plan_gather_parity",
+    "q4rdna_plan_run_host", "q4rdna_plan_set_segments", "q4rdna_plan_run_many", "q4rdna_plan_set_gather", "q4rdna_plan_gather_parity",
     "q4rdna_plan_set_gather_timeout", "q4rdna_ipc_alloc", "q4rdna_ipc_open",
     "q4rdna_ipc_close", "q4rdna_ipc_free",
     "q4rdna_sidecar_open", "q4rdna_sidecar_close", "q4rdna_sidecar_count", "q4rdna_sidecar_entry",
@@ -406,6 +407,13 @@ class Plan:
             self.close()
         except Exception:
             pass
+
+
+def run_plans(plans, stream=None):
+    """Runs the plans in order on the stream with one library call
+    (q4rdna_plan_run_many); each as Plan.run would."""
+    arr = (c_void_p * len(plans))(*[p._h.value for p in plans])
+    check(_lib().q4rdna_plan_run_many(arr, len(plans), _stream_handle(stream)), "plan_run_many")
 
 
 class Sidecar:
