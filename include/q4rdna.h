@@ -65,9 +65,9 @@ typedef struct q4rdna_cfg {
     int reserved[6];
 } q4rdna_cfg;
 
-/* Single calls at B = 1..2 without a norm: let the GEMV start streaming its
- * first weights while the previous kernel on the stream finishes (programmatic
- * dependent launch).  Everything the previous kernels write (x, y, add, the
+/* Single calls at B = 1..2: let the GEMV start streaming its first weights
+ * while the previous kernel on the stream finishes (programmatic dependent
+ * launch).  Everything the previous kernels write (x, y, add, the
  * workspace) is touched only after they complete; only the weight tiles are
  * read early, so the caller guarantees that no kernel still running on the
  * stream writes them (true for weights loaded once, e.g. a sidecar). */
@@ -250,6 +250,13 @@ void q4rdna_plan_destroy(q4rdna_plan *plan);
 q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *x_dev, size_t x_bytes,
                                    const void *y_dev, void *y_host, size_t y_bytes, int segments,
                                    q4rdna_stream_t stream);
+
+/* Launch options of the plan's runs: Q4RDNA_CFG_OVERLAP_PREVIOUS lets each
+ * run start streaming its weights while the previous kernel on the stream
+ * finishes (programmatic dependent launch), as for single calls; the caller
+ * guarantees that no kernel still running on the stream writes the plan's
+ * weight tiles.  B = 1..2 plans only (others ignore it).  0 clears it. */
+q4rdna_status q4rdna_plan_set_flags(q4rdna_plan *plan, int flags);
 
 /* Runs plans[0], plans[1], ... in order on `stream`, each exactly as
  * q4rdna_plan_run does (with its fused gather, if set): one host call for a

@@ -1,14 +1,13 @@
 // Q4_RDNA group-64 GEMV for B200 (sm_100a): shared device helpers, the plan /
 // single-call host side, and the fused tensor-parallel gather.
 //
-// The kernels live in two headers included below:
-//   q4rdna_gemv_i8.cuh  B = 1..2: one warp work item = one 128-row block (four
-//                       32-row tiles) x one K-range of Gs groups, streamed with
-//                       128-bit loads into a register pipeline; int8 tensor-core
-//                       MMAs (mma.sync m16n8k32) sum each group exactly;
-//   q4rdna_gemv_cta.cuh single calls at B = 1..2: one CTA item = 128 rows x a
-//                       K-range split again over the CTA's 8 warps, so a lone
-//                       GEMV keeps the whole GPU streaming;
+// The kernels live in the headers included below:
+//   q4rdna_gemv_i8.cuh  the int8 group math for B = 1..2: a warp streams the four
+//                       32-row tiles of a 128-row block with 128-bit loads into
+//                       a register pipeline; int8 tensor-core MMAs (mma.sync
+//                       m16n8k32) sum each group exactly;
+//   q4rdna_gemv_cta.cuh B = 1..2, single calls and plans: one CTA item = 128 rows
+//                       x a K-range split again over the CTA's 8 warps;
 //   q4rdna_gemv_mb.cuh  B = 3..16: the tile path, one CTA work item of 128 rows,
 //                       the full m16n8k32 fragment over the batch columns.
 // Both scale each 64-element activation group by a power of two, round it to
@@ -125,39 +124,6 @@ __device__ __forceinline__ float split_sumsq(const Task &T, int rb, int b, int B
     return s;
 }
 
-// Last warp to arrive at row block rb: add the split partials in ascending
-// split order, apply the epilogue, store y, and leave the ticket at zero.
-template <bool DUAL, bool NORM = false>
-__device__ __forceinline__ void reduce_splits(const Task &T, int rb, int B, int lane) {
-    constexpr int planes = DUAL ? 2 : 1;
-    __threadfence();
-    // fused RMSNorm: lane b computes batch column b's scale once (B <= 16)
-    float nr_lane = 1.0f;
-    if (NORM && T.gn != nullptr && lane < B) nr_lane = norm_scale(T, split_sumsq(T, rb, lane, B));
-    for (int q4r = 0; q4r < Q4_BLOCK_TILES; ++q4r) {
-        const int row = rb * Q4_BLOCK_ROWS + 32 * q4r + lane;
-        if (row >= T.N) break;
-        for (int b = 0; b < B; ++b) {
-            float s0 = 0.0f, s1 = 0.0f;
-            const float *p0 = T.part + (size_t)b * T.N + row;
-            const size_t split_stride = (size_t)planes * B * T.N;
-#pragma unroll 8
-            for (int sp = 0; sp < T.S; ++sp) {
-                s0 += __ldcg(p0 + sp * split_stride);
-                if (DUAL) s1 += __ldcg(p0 + sp * split_stride + (size_t)B * T.N);
-            }
-            if (NORM && T.gn != nullptr) {
-                const float r = __shfl_sync(0xffffffffu, nr_lane, b);
-                s0 *= r;
-                s1 *= r;
-            }
-            const size_t idx = (size_t)b * T.N + row;
-            put_y(T, idx, finish(s0, s1, T.op, T.add, idx));
-        }
-    }
-    if (lane == 0) atomicExch(&T.ticket[rb], 0u);
-}
-
 __device__ __forceinline__ const Task &find_task(const Launch &L, long long item) {
     if (L.table == nullptr) return L.one;
     int lo = 0, hi = L.ntasks - 1;
@@ -201,49 +167,44 @@ std::atomic<uint64_t> g_launches{0};
 
 struct KernelCfg {
     const void *fn;
-    int threads, warps;  // warps: work items in flight per CTA (1 on the tile path)
+    int threads;
 };
 
-// Batch class of a launch: 0 -> 1 column, 1 -> 2, 2 -> 3..8, 3 -> 9..16.
-constexpr int kBatchClasses = 4;
-int batch_class(int pb) { return pb <= 1 ? 0 : pb == 2 ? 1 : pb <= 8 ? 2 : 3; }
-int class_batch(int bc) { return bc == 0 ? 1 : bc == 1 ? 2 : bc == 2 ? 8 : 16; }
+// Tile-path launch class: 0 -> B = 3..8 (BP = 8), 1 -> B = 9..16 (BP = 16).
+int tile_class(int pb) { return pb <= 8 ? 0 : 1; }
 
 template <bool NORM>
 KernelCfg mb_cfg_n(int pb, bool dual) {
     if (pb <= 8)
-        return dual ? KernelCfg{(const void *)q4_gemv_mb_kernel<8, true, NORM>, kMbThreads, 1}
-                    : KernelCfg{(const void *)q4_gemv_mb_kernel<8, false, NORM>, kMbThreads, 1};
-    return dual ? KernelCfg{(const void *)q4_gemv_mb_kernel<16, true, NORM>, kMbThreads, 1}
-                : KernelCfg{(const void *)q4_gemv_mb_kernel<16, false, NORM>, kMbThreads, 1};
+        return dual ? KernelCfg{(const void *)q4_gemv_mb_kernel<8, true, NORM>, kMbThreads}
+                    : KernelCfg{(const void *)q4_gemv_mb_kernel<8, false, NORM>, kMbThreads};
+    return dual ? KernelCfg{(const void *)q4_gemv_mb_kernel<16, true, NORM>, kMbThreads}
+                : KernelCfg{(const void *)q4_gemv_mb_kernel<16, false, NORM>, kMbThreads};
 }
 
-template <bool DUAL, bool NORM>
-KernelCfg i8_cfg_n(int pb) {
-    return pb <= 1 ? KernelCfg{(const void *)q4_gemv_i8_kernel<1, DUAL, NORM>, kThreads, kWarps}
-                   : KernelCfg{(const void *)q4_gemv_i8_kernel<2, DUAL, NORM>, kThreads, kWarps};
+// The tile path (B >= 3).  dual: the launch holds a SwiGLU task; norm: a
+// fused-RMSNorm task.  Kernels compiled without those paths need fewer
+// registers.  Occupancy and grids are taken from the kernels without a norm
+// (the norm kernels use the same registers +- 5).
+KernelCfg tile_cfg(int pb, bool dual = true, bool norm = false) {
+    return norm ? mb_cfg_n<true>(pb, dual) : mb_cfg_n<false>(pb, dual);
 }
 
-// dual: the launch holds a SwiGLU task; norm: it holds a fused-RMSNorm task.
-// Kernels compiled without those paths need fewer registers.  Occupancy and
-// grids are taken from the kernels without a norm (the norm kernels use the
-// same registers +- 5).
-KernelCfg kernel_cfg(int pb, bool dual = true, bool norm = false) {
-    if (pb >= kTileMinBatch) return norm ? mb_cfg_n<true>(pb, dual) : mb_cfg_n<false>(pb, dual);
-    if (norm) return dual ? i8_cfg_n<true, true>(pb) : i8_cfg_n<false, true>(pb);
-    return dual ? i8_cfg_n<true, false>(pb) : i8_cfg_n<false, false>(pb);
+// The CTA-split kernel (B = 1..2).
+template <bool NORM>
+const void *cta_kernel_n(int pb, bool dual) {
+    if (pb <= 1)
+        return dual ? (const void *)q4_gemv_cta_kernel<1, true, NORM> : (const void *)q4_gemv_cta_kernel<1, false, NORM>;
+    return dual ? (const void *)q4_gemv_cta_kernel<2, true, NORM> : (const void *)q4_gemv_cta_kernel<2, false, NORM>;
 }
-
-// dual: the launch holds a SwiGLU task
-const void *cta_kernel(int pb, bool dual) {
-    if (pb <= 1) return dual ? (const void *)q4_gemv_cta_kernel<1, true> : (const void *)q4_gemv_cta_kernel<1, false>;
-    return dual ? (const void *)q4_gemv_cta_kernel<2, true> : (const void *)q4_gemv_cta_kernel<2, false>;
+const void *cta_kernel(int pb, bool dual, bool norm) {
+    return norm ? cta_kernel_n<true>(pb, dual) : cta_kernel_n<false>(pb, dual);
 }
 
 struct DeviceInfo {
     int sms = 0;
-    int occ[kBatchClasses][2] = {};  // resident CTAs per SM: batch class, SwiGLU (0: unknown)
-    int occ_cta[2][2] = {};          // single-call kernel (B = 1, 2; SwiGLU)
+    int occ_tile[2][2] = {};  // tile path: resident CTAs per SM by tile class, SwiGLU (0: unknown)
+    int occ_cta[2][2] = {};   // CTA-split kernel: by B - 1, SwiGLU
 };
 std::mutex g_dev_mutex;
 DeviceInfo g_dev[kMaxDevices];
@@ -258,22 +219,20 @@ bool device_info(DeviceInfo &out) {
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return false;
         d.sms = sms;
     }
-    for (int bc = 0; bc < kBatchClasses; ++bc)
+    for (int i = 0; i < 2; ++i)
         for (int du = 0; du < 2; ++du) {
-            if (d.occ[bc][du] != 0) continue;
-            const KernelCfg k = kernel_cfg(class_batch(bc), du != 0);
             int o = 0;
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k.fn, k.threads, 0) != cudaSuccess) return false;
-            d.occ[bc][du] = std::max(o, 1);
-        }
-    for (int bb = 0; bb < 2; ++bb)
-        for (int du = 0; du < 2; ++du) {
-            if (d.occ_cta[bb][du] != 0) continue;
-            int o = 0;
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, cta_kernel(bb + 1, du != 0), kThreads, 0) !=
-                cudaSuccess)
-                return false;
-            d.occ_cta[bb][du] = std::max(o, 1);
+            if (d.occ_tile[i][du] == 0) {
+                const KernelCfg k = tile_cfg(i == 0 ? 8 : 16, du != 0);
+                if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k.fn, k.threads, 0) != cudaSuccess) return false;
+                d.occ_tile[i][du] = std::max(o, 1);
+            }
+            if (d.occ_cta[i][du] == 0) {
+                if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, cta_kernel(i + 1, du != 0, false), kThreads, 0) !=
+                    cudaSuccess)
+                    return false;
+                d.occ_cta[i][du] = std::max(o, 1);
+            }
         }
     out = d;
     return true;
@@ -298,34 +257,36 @@ Split make_split(int G, int requested) {
     return Split{(G + Gs - 1) / Gs, Gs};
 }
 
-// Work items in flight on the device: resident warps (batch-1 kernel) or CTAs
-// (tile path).
-long long resident_workers(int pb, bool dual, const DeviceInfo &d) {
-    return (long long)d.sms * d.occ[batch_class(pb)][dual] * kernel_cfg(pb, dual).warps;
+// CTAs resident at once: the CTA-split kernel (B = 1..2) or the tile path.
+long long resident_ctas(int pb, bool dual, const DeviceInfo &d) {
+    if (pb < kTileMinBatch) return (long long)d.sms * d.occ_cta[pb - 1][dual];
+    return (long long)d.sms * d.occ_tile[tile_class(pb)][dual];
 }
 
-// Selector of single calls.
-// B = 1..2 (q4rdna_gemv_cta.cuh): as many CTA K-ranges as fit in ONE wave of
-// resident CTAs (RB * S <= SMs x CTAs per SM), but at least one group per warp
-// (S <= G / 8).  Measured on B200 (bench.py --single --single-sweep, B = 1,
-// split 1..16, us per call), this rule picks the best split within 2% on every
-// config shape: 4096x4096 S = 8 (6.9 us; best 6.8 at S = 4), 12288x4096 S = 3
-// (9.9 us, the best), 4096x12288 S = 9 (10.3 us; best 10.1 at S = 8),
-// 1024x4096 S = 8 (5.5 us; best 5.4), gate+up 12288x4096 S = 3 (14.1 us, the
-// best).  A second wave costs up to 50%: 12288x4096 at S = 4 (384 CTAs)
-// 12.6 us, 4096x12288 at S = 10 (320 CTAs) 15.1 us.
-// B = 3..16 (the tile path): about one item per resident CTA.
+// K-ranges per tensor for a B = 1..2 launch of RB row blocks in total on the
+// CTA-split kernel: as many as fit in ONE wave of resident CTAs
+// (RB * S <= SMs x CTAs per SM), but at least one group per warp (S <= G / 8).
+// Measured on B200 (bench.py --single --single-sweep, B = 1, split 1..16, us
+// per call), this rule picks the best split within 2% on every config shape:
+// 4096x4096 S = 8 (6.9 us; best 6.8 at S = 4), 12288x4096 S = 3 (9.9 us, the
+// best), 4096x12288 S = 9 (10.3 us; best 10.1 at S = 8), 1024x4096 S = 8
+// (5.5 us; best 5.4), gate+up 12288x4096 S = 3 (14.1 us, the best).  A second
+// wave costs up to 50%: 12288x4096 at S = 4 (384 CTAs) 12.6 us, 4096x12288 at
+// S = 10 (320 CTAs) 15.1 us.
+int cta_split(long long total_rb, int G, long long ctas) {
+    const long long S = std::min<long long>(total_rb > 0 ? ctas / total_rb : 1, std::max(1, G / kWarps));
+    return (int)std::max<long long>(S, 1);
+}
+
+// Selector of single calls: the one-wave rule above at B = 1..2; on the tile
+// path (B = 3..16) about one item per resident CTA.
 int select_split_for(int N, int K, int B, int op, const DeviceInfo &d) {
     const int G = K / Q4_GROUP;
     const int RB = (N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
     const bool dual = op == Q4RDNA_OP_SWIGLU;
-    if (B < kTileMinBatch) {
-        const long long ctas = (long long)d.sms * d.occ_cta[B - 1][dual];
-        const long long S = std::min<long long>(ctas / RB, std::max(1, G / kWarps));
-        return make_split(G, (int)std::max<long long>(S, 1)).S;
-    }
-    const long long warps = resident_workers(B, dual, d);
-    const long long S = (warps + RB - 1) / RB;
+    const long long ctas = resident_ctas(B, dual, d);
+    if (B < kTileMinBatch) return make_split(G, cta_split(RB, G, ctas)).S;
+    const long long S = (ctas + RB - 1) / RB;
     return make_split(G, (int)std::min<long long>(S, G)).S;
 }
 
@@ -371,11 +332,9 @@ size_t plan_ws_bytes_for(int N, int B, int S, int op, bool norm) {
            (norm ? align256(sumsq_bytes(N, B, S)) : 0);
 }
 
-// Work items per resident warp (or tile-path CTA) that a plan's split-K choice
-// aims at.  Every split costs partial stores, a fence, an arrival ticket and a
-// reduction per item, which on the Qwen3-8B step cost more than the imbalance
-// of large unsplit items (measured item sizes, one launch: 32 KB 1804 us,
-// 64 KB 949 us, 128 KB 703 us, 256 KB 656 us, unsplit 624-632 us).
+// Work items per resident CTA that a tile-path plan's split-K choice aims at
+// (every split costs partial stores, a fence, an arrival ticket and a
+// reduction per item).
 constexpr double kPlanItemsPerWorker = 2.0;
 
 bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
@@ -387,16 +346,14 @@ q4rdna_status check_shape(int N, int K, int B) {
     return Q4RDNA_OK;
 }
 
+// Persistent grid of a tile-path launch: one CTA per item up to the resident CTAs.
 int grid_for(long long items, int pb, bool dual, const DeviceInfo &d) {
-    const KernelCfg k = kernel_cfg(pb, dual);
-    const long long want = (items + k.warps - 1) / k.warps;
-    const long long cap = (long long)d.sms * d.occ[batch_class(pb)][dual];
-    return (int)std::max<long long>(1, std::min(want, cap));
+    return (int)std::max<long long>(1, std::min(items, resident_ctas(pb, dual, d)));
 }
 
-// pb: batch columns of the launch (1..16).
+// pb: batch columns of the launch (3..16).
 q4rdna_status launch(const Launch &L, int grid, int pb, bool dual, cudaStream_t stream, bool norm = false) {
-    const KernelCfg k = kernel_cfg(pb, dual, norm);
+    const KernelCfg k = tile_cfg(pb, dual, norm);
     Launch arg = L;
     void *args[] = {&arg};
     if (cudaLaunchKernel(k.fn, dim3(grid), dim3(k.threads), args, 0, stream) != cudaSuccess)
@@ -408,7 +365,7 @@ q4rdna_status launch(const Launch &L, int grid, int pb, bool dual, cudaStream_t 
 
 // The CTA-split kernel (q4rdna_gemv_cta.cuh, B = 1..2): one CTA per item of
 // L (total_items CTAs); overlap: programmatic dependent launch.
-q4rdna_status launch_cta(const Launch &L, int pb, bool dual, cudaStream_t stream, bool overlap = false) {
+q4rdna_status launch_cta(const Launch &L, int pb, bool dual, bool norm, cudaStream_t stream, bool overlap = false) {
     Launch arg = L;
     void *args[] = {&arg};
     cudaLaunchConfig_t lc = {};
@@ -422,7 +379,7 @@ q4rdna_status launch_cta(const Launch &L, int pb, bool dual, cudaStream_t stream
         lc.attrs = at;
         lc.numAttrs = 1;
     }
-    if (cudaLaunchKernelExC(&lc, cta_kernel(pb, dual), args) != cudaSuccess) return Q4RDNA_ERR_CUDA;
+    if (cudaLaunchKernelExC(&lc, cta_kernel(pb, dual, norm), args) != cudaSuccess) return Q4RDNA_ERR_CUDA;
     if (cudaGetLastError() != cudaSuccess) return Q4RDNA_ERR_CUDA;
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return Q4RDNA_OK;
@@ -474,8 +431,9 @@ q4rdna_status gemv_common(int op, const uint8_t *w, const uint8_t *w2, const flo
     T.nss = (gn != nullptr && sp.S > 1) ? part + partial_bytes(N, B, sp.S, op) / sizeof(float) : nullptr;
     L.total_items = (long long)RB * sp.S;
     const bool dual = op == Q4RDNA_OP_SWIGLU;
-    if (B < kTileMinBatch && gn == nullptr)  // one CTA per (row block, K-range) (q4rdna_gemv_cta.cuh)
-        return launch_cta(L, B, dual, stream, cfg != nullptr && (cfg->flags & Q4RDNA_CFG_OVERLAP_PREVIOUS));
+    if (B < kTileMinBatch)  // one CTA per (row block, K-range) (q4rdna_gemv_cta.cuh)
+        return launch_cta(L, B, dual, gn != nullptr, stream,
+                          cfg != nullptr && (cfg->flags & Q4RDNA_CFG_OVERLAP_PREVIOUS));
     return launch(L, grid_for(L.total_items, B, dual, d), B, dual, stream, gn != nullptr);
 }
 
@@ -497,6 +455,9 @@ constexpr int kGatherTries = 1 << 22;  // x ~0.5 us sleep: about 2 s
 constexpr unsigned kFaultGatherTimeout = 2u;
 
 __global__ void q4_gather_signal_kernel(const __grid_constant__ GatherSignal a) {
+    // the next plan, when launched with programmatic dependent launch, may start
+    // streaming its weights now; it reads nothing else before this kernel ends
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int p = threadIdx.x;
     if (p >= a.world) return;
     // the plan kernel's stores (peer ones included) precede this kernel in stream
@@ -610,7 +571,8 @@ struct q4rdna_plan {
     int count = 0, B = 1, nb = 1, grid = 1;
     bool dual = false;  // the plan holds a SwiGLU task
     bool norm = false;  // the plan holds a fused-RMSNorm task
-    bool cta = false;   // runs on the CTA-split kernel (one CTA per item), else the persistent warp-item kernel
+    bool cta = false;   // B = 1..2: the CTA-split kernel (one CTA per item), else the tile path
+    bool overlap = false;  // q4rdna_plan_set_flags(Q4RDNA_CFG_OVERLAP_PREVIOUS): programmatic dependent launch
     long long items = 0;
     Task *table = nullptr;     // device
     void *workspace = nullptr; // device
@@ -662,7 +624,7 @@ struct q4rdna_plan {
 namespace {
 // One launch of (a segment of) a plan on its kernel.
 q4rdna_status plan_launch(const q4rdna_plan *plan, const Launch &L, int grid, cudaStream_t stream) {
-    if (plan->cta) return launch_cta(L, plan->nb, plan->dual, stream);
+    if (plan->cta) return launch_cta(L, plan->nb, plan->dual, plan->norm, stream, plan->overlap);
     return launch(L, grid, plan->nb, plan->dual, stream, plan->norm);
 }
 
@@ -767,28 +729,22 @@ q4rdna_status plan_create_rdna(const q4rdna_gemv_desc *descs, int count, int B, 
     size_t ws_total = 0;
     long long items = 0;
     uint64_t wbytes = 0, abytes = 0;
-    // Split-K only as far as the whole plan needs it: each task gets the split
-    // that gives the plan about kPlanItemsPerWorker items per resident warp
-    // (CTA on the tile path).
+    // Split-K only as far as the whole plan needs it.  B = 1..2 (the CTA-split
+    // kernel, one CTA per (row block, K-range)): as many K-ranges per tensor as
+    // fit one wave of resident CTAs over all the plan's row blocks, at least one
+    // group per warp (cta_split) -- the Qwen3-8B step's 10944 row blocks run
+    // unsplit.  B = 3..16 (the tile path): about kPlanItemsPerWorker items per
+    // resident CTA.
     long long total_rb = 0;
     bool any_dual_task = false;
     for (int i = 0; i < count; ++i) {
         if (descs[i].N > 0) total_rb += (descs[i].N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
         any_dual_task = any_dual_task || descs[i].op == Q4RDNA_OP_SWIGLU;
     }
-    const long long workers = resident_workers(B, any_dual_task, d);
-    const double want_items = kPlanItemsPerWorker * (double)workers;
-    const int plan_split = total_rb > 0 ? (int)std::max(1.0, std::ceil(want_items / (double)total_rb)) : 1;
-    // Plans too small for unsplit warp items (plan_split > 1: a tensor-parallel
-    // rank's shards, a decoder stage) run on the CTA-split kernel at B = 1..2
-    // (no fused norm): a CTA per (row block, K-range) with the K-range split
-    // again over its 8 warps, and as many K-ranges per tensor as fit one wave
-    // of resident CTAs (at least one group per warp).
-    bool any_norm_task = false;
-    for (int i = 0; i < count; ++i) any_norm_task = any_norm_task || descs[i].norm_weight != nullptr;
-    const bool cta = B < kTileMinBatch && !any_norm_task && plan_split > 1;
-    const long long ctas = (long long)d.sms * d.occ_cta[std::min(B, 2) - 1][any_dual_task];
-    const int cta_split = total_rb > 0 ? (int)std::max<long long>(1, ctas / total_rb) : 1;
+    const bool cta = B < kTileMinBatch;
+    const long long ctas = resident_ctas(B, any_dual_task, d);
+    const double want_items = kPlanItemsPerWorker * (double)ctas;
+    const int tile_split = total_rb > 0 ? (int)std::max(1.0, std::ceil(want_items / (double)total_rb)) : 1;
     for (int i = 0; i < count; ++i) {
         const q4rdna_gemv_desc &e = descs[i];
         q4rdna_status st = check_shape(e.N, e.K, B);
@@ -803,7 +759,7 @@ q4rdna_status plan_create_rdna(const q4rdna_gemv_desc *descs, int count, int B, 
         const int planes = e.op == Q4RDNA_OP_SWIGLU ? 2 : 1;
         const int G = e.K / Q4_GROUP;
         const int RB = (e.N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
-        const int req = e.split > 0 ? e.split : cta ? std::min(cta_split, std::max(1, G / kWarps)) : std::min(plan_split, G);
+        const int req = e.split > 0 ? e.split : cta ? cta_split(total_rb, G, ctas) : std::min(tile_split, G);
         const Split sp = make_split(G, req);
         Task &T = host[i];
         T.w = e.tiles; T.w2 = e.gate_tiles; T.x = e.x; T.add = e.add; T.y = e.y;
@@ -1295,6 +1251,12 @@ q4rdna_status q4rdna_plan_run_many(q4rdna_plan *const *plans, int count, q4rdna_
         const q4rdna_status st = q4rdna_plan_run(plans[i], stream);
         if (st != Q4RDNA_OK) return st;
     }
+    return Q4RDNA_OK;
+}
+
+q4rdna_status q4rdna_plan_set_flags(q4rdna_plan *plan, int flags) {
+    if (plan == nullptr || (flags & ~Q4RDNA_CFG_OVERLAP_PREVIOUS) != 0) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    plan->overlap = (flags & Q4RDNA_CFG_OVERLAP_PREVIOUS) != 0;
     return Q4RDNA_OK;
 }
 

@@ -1,6 +1,5 @@
 // CTA-split GEMV for B = 1..2 (included into q4rdna_gemv.cu inside namespace
-// q4, after q4rdna_gemv_i8.cuh): single calls, and plans whose row blocks are
-// too few to give every resident warp a whole-K item.
+// q4, after q4rdna_gemv_i8.cuh): every single call and every plan at B <= 2.
 //
 // A lone GEMV has too few rows to keep every warp busy with whole-K items: a
 // warp streams one group (4.3 KB) per DRAM round trip, so an item of 64 groups
@@ -15,8 +14,17 @@
 //     adds them in ascending order with all 256 threads and applies the add /
 //     SwiGLU epilogue.
 // Accumulation order of an output: exact int32 inside a group; the groups of a
-// warp in ascending order (as in the batch-1 kernel); warps in ascending order;
-// CTA K-ranges in ascending order.  Deterministic: no data atomics.
+// warp in ascending order, sum = fma(scale / 16, v * 2^e, sum); warps in
+// ascending order; CTA K-ranges in ascending order.  The fused RMSNorm's sum of
+// h^2 follows the same order (groups, warps, K-ranges), and its scale
+// 1 / sqrt(sum / K + eps) multiplies each output once, before the epilogue.
+// Deterministic: no data atomics.
+//
+// A large plan (the Qwen3-8B step: 10944 row blocks) is one wave after another
+// of these CTAs; measured on B200 it matches the persistent warp-item design it
+// replaced (625 vs 630 us per step) and beats it when the rows per tensor are
+// few (a tensor-parallel rank's shards: 325 vs 379 us at 2 ranks, 95 vs 137 us
+// at 8).
 //
 // Programmatic dependent launch (Q4RDNA_CFG_OVERLAP_PREVIOUS): every CTA lets
 // the next kernel of the stream launch at once, and waits for the previous
@@ -39,11 +47,13 @@ template <int BB>
 struct CtaSmem {
     I8X<BB> xs[kWarps][2];
     float red[kWarps][2][4][BB][32];  // [warp][plane][q][b][lane]
+    float ssq[kWarps][BB];            // fused RMSNorm: each warp's sum of h^2 per batch column
     unsigned last;
 };
 
-// One CTA item of task T: row block rb, K-range sc.
-template <int BB, bool DUAL>
+// One CTA item of task T: row block rb, K-range sc.  NORM: the kernel has the
+// fused-RMSNorm path (used by tasks with a norm weight, T.gn != null).
+template <int BB, bool DUAL, bool NORM>
 __device__ __forceinline__ void cta_item(const Task &T, int B, int rb, int sc, CtaSmem<BB> &sm) {
     constexpr int planes = DUAL ? 2 : 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -60,6 +70,10 @@ __device__ __forceinline__ void cta_item(const Task &T, int B, int rb, int sc, C
         for (int q = 0; q < 4; ++q)
 #pragma unroll
             for (int b = 0; b < BB; ++b) acc[pl][q][b] = 0.0f;
+    const bool norm = NORM && T.gn != nullptr;
+    float iss[BB];  // fused RMSNorm: this warp's sum of h^2 per batch column, groups ascending
+#pragma unroll
+    for (int b = 0; b < BB; ++b) iss[b] = 0.0f;
 
     if (ng > 0) {
         I8Sel sel;
@@ -86,11 +100,19 @@ __device__ __forceinline__ void cta_item(const Task &T, int B, int rb, int sc, C
         StepBufI8 buf;
         load_step_i8(buf, base0, c, h);  // weights: not written by the previous kernels
         asm volatile("griddepcontrol.wait;" ::: "memory");
-        float2 xv[BB], gv = make_float2(1.0f, 1.0f);
+        // fused RMSNorm: the group is prepared as h * g (g = 1 without a norm weight)
+        auto fetch_g = [&](int g) -> float2 {
+            return norm ? __ldg(reinterpret_cast<const float2 *>(T.gn + (size_t)g * Q4_GROUP) + lane)
+                        : make_float2(1.0f, 1.0f);
+        };
+        float2 xv[BB], gv = NORM ? fetch_g(g0) : make_float2(1.0f, 1.0f);
         cta_fetch_x<BB>(T, B, g0, lane, xv);
 #pragma unroll
-        for (int b = 0; b < BB; ++b) prep_group_i8<false>(xv[b], gv, false, xs[0].xq[b], &xs[0].up[b], &xs[0].ss[b], lane);
-        if (ng > 1) cta_fetch_x<BB>(T, B, g0 + 1, lane, xv);
+        for (int b = 0; b < BB; ++b) prep_group_i8<NORM>(xv[b], gv, norm, xs[0].xq[b], &xs[0].up[b], &xs[0].ss[b], lane);
+        if (ng > 1) {
+            cta_fetch_x<BB>(T, B, g0 + 1, lane, xv);
+            if (NORM) gv = fetch_g(g0 + 1);
+        }
         __syncwarp();
         int par = 0;
         for (int st = 0; st < nsteps; ++st) {
@@ -99,13 +121,20 @@ __device__ __forceinline__ void cta_item(const Task &T, int B, int rb, int sc, C
             RegSource src(buf, step_tile(st + 1 < nsteps ? st + 1 : st), c, h);
             if (tt == 0) {
                 mma_step_i8<BB>(src, xs[par], acc[0], lane, sel);
+                if (NORM) {
+#pragma unroll
+                    for (int b = 0; b < BB; ++b) iss[b] += xs[par].ss[b];
+                }
                 if (gl + 1 < ng) {
                     // the next group's activation into the other buffer
 #pragma unroll
                     for (int b = 0; b < BB; ++b)
-                        prep_group_i8<false>(xv[b], gv, false, xs[par ^ 1].xq[b], &xs[par ^ 1].up[b],
-                                             &xs[par ^ 1].ss[b], lane);
-                    if (gl + 2 < ng) cta_fetch_x<BB>(T, B, g0 + gl + 2, lane, xv);
+                        prep_group_i8<NORM>(xv[b], gv, norm, xs[par ^ 1].xq[b], &xs[par ^ 1].up[b],
+                                            &xs[par ^ 1].ss[b], lane);
+                    if (gl + 2 < ng) {
+                        cta_fetch_x<BB>(T, B, g0 + gl + 2, lane, xv);
+                        if (NORM) gv = fetch_g(g0 + gl + 2);
+                    }
                 }
             } else {
                 mma_step_i8<BB>(src, xs[par], acc[DUAL ? 1 : 0], lane, sel);
@@ -126,7 +155,18 @@ __device__ __forceinline__ void cta_item(const Task &T, int B, int rb, int sc, C
         for (int q = 0; q < 4; ++q)
 #pragma unroll
             for (int b = 0; b < BB; ++b) sm.red[warp][pl][q][b][lane] = acc[pl][q][b];
+    if (NORM && lane == 0) {
+#pragma unroll
+        for (int b = 0; b < BB; ++b) sm.ssq[warp][b] = iss[b];
+    }
     __syncthreads();
+    // fused RMSNorm: the CTA's sum of h^2 of batch column b over its K-range, warps ascending
+    auto cta_sumsq = [&](int b) -> float {
+        float q = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) q += sm.ssq[w][b];
+        return q;
+    };
 
     // thread -> outputs (q, b, ln) of the block: row = tile (ln >> 3) of the
     // block, row in tile 16 ((ln >> 2) & 1) + (ln & 3) + 4 q
@@ -148,6 +188,11 @@ __device__ __forceinline__ void cta_item(const Task &T, int B, int rb, int sc, C
         }
         const size_t idx = (size_t)b * T.N + row;
         if (T.S == 1) {
+            if (norm) {
+                const float r = norm_scale(T, cta_sumsq(b));
+#pragma unroll
+                for (int pl = 0; pl < planes; ++pl) v[pl] *= r;
+            }
             put_y(T, idx, finish(v[0], v[planes - 1], T.op, T.add, idx));
         } else {
 #pragma unroll
@@ -157,6 +202,7 @@ __device__ __forceinline__ void cta_item(const Task &T, int B, int rb, int sc, C
     if (T.S == 1) return;
 
     // K-ranges of several CTAs: the last one to arrive adds them in order
+    if (norm && threadIdx.x < B) __stcg(&T.nss[((size_t)rb * T.S + sc) * B + threadIdx.x], cta_sumsq(threadIdx.x));
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) sm.last = atomicAdd(&T.ticket[rb], 1u) == (unsigned)(T.S - 1) ? 1u : 0u;
@@ -175,14 +221,20 @@ __device__ __forceinline__ void cta_item(const Task &T, int B, int rb, int sc, C
             for (int sp = 0; sp < T.S; ++sp) s += __ldcg(&T.part[(size_t)sp * split_stride + (size_t)pl * B * T.N + idx]);
             v[pl] = s;
         }
+        if (norm) {  // the splits' sums of h^2 in ascending split order
+            const float r = norm_scale(T, split_sumsq(T, rb, b, B));
+#pragma unroll
+            for (int pl = 0; pl < planes; ++pl) v[pl] *= r;
+        }
         put_y(T, idx, finish(v[0], v[planes - 1], T.op, T.add, idx));
     }
     if (threadIdx.x == 0) atomicExch(&T.ticket[rb], 0u);
 }
 
 // One CTA per item (not persistent).  HAS_DUAL = false: the launch holds no
-// SwiGLU task, so that path is compiled out.
-template <int BB, bool HAS_DUAL>
+// SwiGLU task; NORM = false: no fused-RMSNorm task; those paths are compiled
+// out.
+template <int BB, bool HAS_DUAL, bool NORM>
 __global__ void __launch_bounds__(kThreads, 2) q4_gemv_cta_kernel(const __grid_constant__ Launch L) {
     __shared__ CtaSmem<BB> sm;
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -191,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 2) q4_gemv_cta_kernel(const __grid_c
     const int local = (int)(it - T.item_begin);
     const int rb = local / T.S, sc = local % T.S;
     if (HAS_DUAL && T.op == Q4RDNA_OP_SWIGLU)
-        cta_item<BB, true>(T, L.B, rb, sc, sm);
+        cta_item<BB, true, NORM>(T, L.B, rb, sc, sm);
     else
-        cta_item<BB, false>(T, L.B, rb, sc, sm);
+        cta_item<BB, false, NORM>(T, L.B, rb, sc, sm);
 }

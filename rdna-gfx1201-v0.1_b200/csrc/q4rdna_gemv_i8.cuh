@@ -1,7 +1,7 @@
-// int8 tensor-core GEMV for B = 1..2 (included into q4rdna_gemv.cu inside
-// namespace q4).  A warp work item is one 128-row block (four 32-row tiles) x
-// one K-range of Gs groups; the warp streams its tiles with 128-bit loads
-// through a register pipeline.
+// int8 tensor-core group math for B = 1..2 (included into q4rdna_gemv.cu
+// inside namespace q4; the kernel built on it is q4rdna_gemv_cta.cuh).  A warp
+// streams the four 32-row tiles of a 128-row block, one group (64 columns) per
+// step, with 128-bit loads through a register pipeline.
 //
 //   * codes: a nibble in the HIGH half of a byte is exactly 16 * code as an s8,
 //     so a 32-bit code word (4 rows x 2 columns) becomes two A registers with
@@ -45,14 +45,6 @@ struct __align__(16) I8X {
     float up[BB];               // 2^e: undoes the group's power-of-two scaling
     float ss[BB];               // fused RMSNorm: the group's sum of h^2
 };
-
-// Branch-free, so that the compiler can interleave it with the previous
-// group's MMAs (see run_item_i8).
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
 
 // Activation scaling shared by both int8 kernels.  E = biased exponent of the
 // group's largest |x| = m, clamped to >= 30 so that both 2^(156 - E) and
@@ -159,10 +151,10 @@ __device__ __forceinline__ void load_step_i8(StepBufI8 &b, const uint8_t *tile, 
     for (int q = 0; q < 4; ++q) b.s[q] = ld_stream2(sp + 8 * q);
 }
 
-// Where a step's code and scale words come from.  RegSource: the register
-// pipeline (slot m of the buffer is refilled from the following step's tile as
-// soon as it is consumed, so one step of loads is always in flight and the loop
-// has no branches).  SmemSource: a staged tile in shared memory.
+// Where a step's code and scale words come from: the register pipeline (slot m
+// of the buffer is refilled from the following step's tile as soon as it is
+// consumed, so one step of loads is always in flight and the loop has no
+// branches).
 struct RegSource {
     StepBufI8 &buf;
     const uint8_t *nq, *ns;  // following step: code and scale addresses of this lane
@@ -180,17 +172,6 @@ struct RegSource {
         buf.q[m] = ld_stream16(nq + 128 * m);
         return cur;
     }
-};
-
-struct SmemSource {
-    const uint8_t *q, *s;
-    __device__ __forceinline__ SmemSource(const uint8_t *tile, int c, int h)
-        : q(tile + Q4_SCALE_BYTES + 32 * c + 16 * h), s(tile + 32 * h + 2 * c) {}
-    __device__ __forceinline__ void scales(uint32_t (&sw)[4]) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) sw[k] = *reinterpret_cast<const unsigned short *>(s + 8 * k);
-    }
-    __device__ __forceinline__ uint4 codes(int m) { return *reinterpret_cast<const uint4 *>(q + 128 * m); }
 };
 
 // One group of one tensor: 32 (BB = 1) int8 MMAs per warp, exact int32 digit
@@ -270,253 +251,5 @@ __device__ __forceinline__ void mma_step_i8(Src &src, const I8X<BB> &sm, float (
             // v * 2^e is exact (a power of two, in range), so this is one rounding
             acc[q][b] = fmaf(sc, v * sm.up[b], acc[q][b]);
         }
-    }
-}
-
-// Epilogue of one item in the int8 layout: lane rows tile_row*32 + 16h + c + 4q.
-// iss: fused RMSNorm (NORM kernels), the item's sum of h^2 per batch column.
-template <int BB, bool DUAL, bool NORM>
-__device__ __forceinline__ void finish_rows_i8(const Task &T, int rb, int s, int B, float (&acc)[2][4][BB],
-                                               const float (&iss)[BB], int lane, bool valid, int tile_row, int h,
-                                               int c) {
-    const int row0 = tile_row * Q4_TILE_ROWS + 16 * h + c;
-    if (T.S == 1) {
-        if (valid) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-#pragma unroll
-                for (int b = 0; b < BB; ++b) {
-                    if (b >= B) continue;
-                    const size_t idx = (size_t)b * T.N + row0 + 4 * q;
-                    float v = acc[0][q][b], gate = acc[DUAL ? 1 : 0][q][b];
-                    if (NORM && T.gn != nullptr) {
-                        const float r = norm_scale(T, iss[b]);  // the compiler hoists it out of q
-                        v *= r;
-                        gate *= r;
-                    }
-                    put_y(T, idx, finish(v, gate, T.op, T.add, idx));
-                }
-        }
-        return;
-    }
-    constexpr int planes = DUAL ? 2 : 1;
-    if (NORM && T.gn != nullptr && lane == 0) {
-#pragma unroll
-        for (int b = 0; b < BB; ++b)
-            if (b < B) __stcg(&T.nss[((size_t)rb * T.S + s) * B + b], iss[b]);
-    }
-    if (valid) {
-#pragma unroll
-        for (int pl = 0; pl < planes; ++pl)
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-#pragma unroll
-                for (int b = 0; b < BB; ++b) {
-                    if (b >= B) continue;
-                    __stcg(&T.part[(((size_t)s * planes + pl) * B + b) * T.N + row0 + 4 * q], acc[pl][q][b]);
-                }
-    }
-    __threadfence();
-    __syncwarp();
-    unsigned prev = 0;
-    if (lane == 0) prev = atomicAdd(&T.ticket[rb], 1u);
-    prev = __shfl_sync(0xffffffffu, prev, 0);
-    if (prev != (unsigned)(T.S - 1)) return;
-    reduce_splits<DUAL, NORM>(T, rb, B, lane);
-}
-
-// This lane's tile of step 0 of an item, and the item's first group.  Rows past
-// N read the block's first row tile instead (always present), so every load is
-// in bounds and unconditional; those rows are never stored.
-__device__ __forceinline__ const uint8_t *item_tile0(const Task &T, int local, int lane, int *g0_out) {
-    const int rb = local / T.S, sp = local % T.S;
-    const int g0 = sp * T.Gs;
-    const int t = lane >> 3;
-    int tile_row = rb * Q4_BLOCK_TILES + t;
-    if (tile_row >= (T.N >> 5)) tile_row = rb * Q4_BLOCK_TILES;
-    if (g0_out) *g0_out = g0;
-    return T.w + ((size_t)tile_row * T.G + g0) * Q4_TILE_BYTES;
-}
-
-// Flat cursor over the warp's activation groups (its items in order, each with
-// its groups): the raw f32 of the group it points at is fetched two groups
-// ahead of the group being multiplied.
-struct XCursor {
-    long long it;      // item (>= total: past the warp's last group)
-    int g, ng, g0, K;  // group within the item, the item's groups, first group, columns
-    const float *x;
-    const float *gn;   // fused RMSNorm weight, or null
-};
-
-__device__ __forceinline__ void xc_load(const Launch &L, XCursor &c) {
-    if (c.it >= L.total_items) return;
-    const Task &T = find_task(L, c.it);
-    const int local = (int)(c.it - T.item_begin);
-    c.g0 = (local % T.S) * T.Gs;
-    c.ng = min(T.Gs, T.G - c.g0);
-    c.g = 0;
-    c.K = T.K;
-    c.x = T.x;
-    c.gn = T.gn;
-}
-
-__device__ __forceinline__ void xc_advance(const Launch &L, XCursor &c, long long nw) {
-    if (c.it >= L.total_items) return;
-    if (++c.g >= c.ng) {
-        c.it += nw;
-        xc_load(L, c);
-    }
-}
-
-template <int BB, bool NORM>
-__device__ __forceinline__ void xc_fetch(const Launch &L, const XCursor &c, int lane, float2 (&xv)[BB], float2 &gv,
-                                         bool &norm) {
-    if (c.it >= L.total_items) return;
-#pragma unroll
-    for (int b = 0; b < BB; ++b)
-        if (b < L.B)
-            xv[b] = __ldg(reinterpret_cast<const float2 *>(c.x + (size_t)b * c.K + (size_t)(c.g0 + c.g) * Q4_GROUP) +
-                          lane);
-    if (NORM) {
-        // a predicated load, not a branch: tasks without a norm take g = 1
-        norm = c.gn != nullptr;
-        const float2 *gp = reinterpret_cast<const float2 *>((norm ? c.gn : c.x) + (size_t)(c.g0 + c.g) * Q4_GROUP) + lane;
-        const float2 g = __ldg(gp);
-        gv = norm ? g : make_float2(1.0f, 1.0f);
-    }
-}
-
-// Per-warp state carried from item to item.
-template <int BB>
-struct I8Pipe {
-    StepBufI8 buf;   // code and scale words of the next step (register pipeline)
-    float2 xv[BB];   // raw x of the next group to prepare
-    float2 gv;       // fused RMSNorm: the norm weight of that group's columns
-    bool norm;       // that group belongs to a fused-RMSNorm task
-    XCursor xc;      // the group whose raw x is in xv
-    int par;         // activation buffer holding the group being multiplied
-};
-
-// Prepare the raw x in P.xv (the cursor's group) into activation buffer xs;
-// past the warp's last group it writes a spare buffer that is never read.
-template <int BB, bool NORM>
-__device__ __forceinline__ void prep_ahead(I8Pipe<BB> &P, I8X<BB> &xs, int lane) {
-#pragma unroll
-    for (int b = 0; b < BB; ++b) prep_group_i8<NORM>(P.xv[b], P.gv, P.norm, xs.xq[b], &xs.up[b], &xs.ss[b], lane);
-}
-
-template <int BB, bool DUAL, bool NORM>
-__device__ __forceinline__ void run_item_i8(const Launch &L, const Task &T, int local, I8X<BB> (&xs)[2], int lane,
-                                            const I8Sel &sel, I8Pipe<BB> &P, const Task *nT, int nlocal,
-                                            long long nw) {
-    const int rb = local / T.S, s = local % T.S;
-    const int g0 = s * T.Gs, ng = min(T.Gs, T.G - g0);
-    const int grp = lane >> 2, c = lane & 3, t = grp >> 1, h = grp & 1;
-    const int tile_row = rb * Q4_BLOCK_TILES + t;
-    const bool valid = tile_row < (T.N >> 5);
-    const uint8_t *base0 = item_tile0(T, local, lane, nullptr);
-    const uint8_t *base1 = DUAL ? T.w2 + (base0 - T.w) : base0;
-    const uint8_t *after = nT ? item_tile0(*nT, nlocal, lane, nullptr)
-                              : (DUAL ? base1 : base0) + (size_t)(ng - 1) * Q4_TILE_BYTES;
-    const int nsteps = ng * (DUAL ? 2 : 1);
-    (void)g0;
-
-    float acc[2][4][BB];
-#pragma unroll
-    for (int pl = 0; pl < 2; ++pl)
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-#pragma unroll
-            for (int b = 0; b < BB; ++b) acc[pl][q][b] = 0.0f;
-    float iss[BB];
-#pragma unroll
-    for (int b = 0; b < BB; ++b) iss[b] = 0.0f;
-
-    for (int st = 0; st < nsteps; ++st) {
-        const int tt = DUAL ? (st & 1) : 0;
-        const uint8_t *next;
-        if (st + 1 < nsteps) {
-            const int tn = DUAL ? ((st + 1) & 1) : 0, gn = DUAL ? ((st + 1) >> 1) : st + 1;
-            next = (tn ? base1 : base0) + (size_t)gn * Q4_TILE_BYTES;
-        } else {
-            next = after;
-        }
-        RegSource src(P.buf, next, c, h);
-        I8X<BB> &cur = xs[P.par];
-        if (tt == 0) {
-            mma_step_i8<BB>(src, cur, acc[0], lane, sel);
-            if (NORM) {
-#pragma unroll
-                for (int b = 0; b < BB; ++b) iss[b] += cur.ss[b];  // groups in ascending order
-            }
-            // The next group's activation goes into the other buffer while the
-            // MMAs above drain: no branch in between, so the compiler can
-            // interleave the two independent chains.
-            prep_ahead<BB, NORM>(P, xs[P.par ^ 1], lane);
-        } else {
-            mma_step_i8<BB>(src, cur, acc[1], lane, sel);
-        }
-        if (!DUAL || tt == 1) {
-            // end of the group: the prepared buffer becomes current for everyone,
-            // and no lane still reads the old one when it is rewritten next
-            __syncwarp();
-            P.par ^= 1;
-            xc_advance(L, P.xc, nw);
-            xc_fetch<BB, NORM>(L, P.xc, lane, P.xv, P.gv, P.norm);
-        }
-    }
-    if (DUAL)
-        finish_rows_i8<BB, true, NORM>(T, rb, s, L.B, acc, iss, lane, valid, tile_row, h, c);
-    else
-        finish_rows_i8<BB, false, NORM>(T, rb, s, L.B, acc, iss, lane, valid, tile_row, h, c);
-}
-
-// HAS_DUAL = false: the launch holds no SwiGLU task, so the SwiGLU path (and its
-// registers) is compiled out.
-// NORM = false: the launch holds no fused-RMSNorm task, so that path is compiled out.
-template <int BB, bool HAS_DUAL, bool NORM>
-__global__ void __launch_bounds__(kThreads, BB <= 2 ? 2 : 1) q4_gemv_i8_kernel(const __grid_constant__ Launch L) {
-    __shared__ I8X<BB> xsm[kWarps][2];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long nw = (long long)gridDim.x * kWarps;
-    long long it = (long long)blockIdx.x * kWarps + warp;
-    if (it >= L.total_items) return;
-    I8Sel sel;
-    {
-        const int n = lane >> 2;  // this lane's B column
-        sel.a = sel_one(n >> 1, (n & 1) ? 0 : 1);
-        sel.b2 = sel_one(n >> 1, 2);
-        sel.b3 = sel_one(n >> 1, 3);
-        sel.bcol_odd = n & 1;
-    }
-    const int c = lane & 3, h = (lane >> 2) & 1;
-    I8X<BB>(&xs)[2] = xsm[warp];
-    I8Pipe<BB> P;
-    P.par = 0;
-    {
-        const Task &T = find_task(L, it);
-        load_step_i8(P.buf, item_tile0(T, (int)(it - T.item_begin), lane, nullptr), c, h);
-    }
-#pragma unroll
-    for (int b = 0; b < BB; ++b) P.xv[b] = make_float2(0.0f, 0.0f);
-    P.gv = make_float2(0.0f, 0.0f);
-    P.norm = false;
-    // the warp's first group into buffer 0, the second group's raw x in flight
-    P.xc.it = it;
-    xc_load(L, P.xc);
-    xc_fetch<BB, NORM>(L, P.xc, lane, P.xv, P.gv, P.norm);
-    prep_ahead<BB, NORM>(P, xs[0], lane);
-    xc_advance(L, P.xc, nw);
-    xc_fetch<BB, NORM>(L, P.xc, lane, P.xv, P.gv, P.norm);
-    __syncwarp();
-    for (; it < L.total_items; it += nw) {
-        const Task &T = find_task(L, it);
-        const long long nit = it + nw;
-        const Task *nT = nit < L.total_items ? &find_task(L, nit) : nullptr;
-        const int nlocal = nT ? (int)(nit - nT->item_begin) : 0;
-        if (HAS_DUAL && T.op == Q4RDNA_OP_SWIGLU)
-            run_item_i8<BB, true, NORM>(L, T, (int)(it - T.item_begin), xs, lane, sel, P, nT, nlocal, nw);
-        else
-            run_item_i8<BB, false, NORM>(L, T, (int)(it - T.item_begin), xs, lane, sel, P, nT, nlocal, nw);
     }
 }

@@ -84,6 +84,7 @@ def _bind(lib):
         "q4rdna_plan_run_host": (c_int, [P, P, P, c_size_t, P, P, c_size_t, c_int, P]),
         "q4rdna_plan_set_segments": (c_int, [P, c_int]),
         "q4rdna_plan_run_many": (c_int, [POINTER(P), c_int, P]),
+        "q4rdna_plan_set_flags": (c_int, [P, c_int]),
         "q4rdna_plan_set_gather": (c_int, [P, c_int, c_int, P, c_size_t, POINTER(P), POINTER(P), POINTER(P)]),
         "q4rdna_plan_gather_parity": (c_int, [P]),
         "q4rdna_plan_set_gather_timeout": (c_int, [P, ctypes.c_uint32]),
@@ -138,7 +139,7 @@ SYMBOLS = [
     "q4rdna_gemv_noalloc",
     "q4rdna_q4k_bytes", "q4rdna_q4k_gemv", "q4rdna_q4k_dequant_f32",
     "q4rdna_plan_create", "q4rdna_plan_run", "q4rdna_plan_get_info", "q4rdna_plan_destroy",
-    "q4rdna_plan_run_host", "q4rdna_plan_set_segments", "q4rdna_plan_run_many", "q4rdna_plan_set_gather", "q4rdna_plan_gather_parity",
+    "q4rdna_plan_run_host", "q4rdna_plan_set_segments", "q4rdna_plan_run_many", "q4rdna_plan_set_flags", "q4rdna_plan_set_gather", "q4rdna_plan_gather_parity",
     "q4rdna_plan_set_gather_timeout", "q4rdna_ipc_alloc", "q4rdna_ipc_open",
     "q4rdna_ipc_close", "q4rdna_ipc_free",
     "q4rdna_sidecar_open", "q4rdna_sidecar_close", "q4rdna_sidecar_count", "q4rdna_sidecar_entry",
@@ -373,6 +374,11 @@ class Plan:
     def run(self, stream=None):
         check(_lib().q4rdna_plan_run(self._h, _stream_handle(stream)), "plan_run")
 
+    def set_flags(self, flags: int):
+        """Launch options of the runs (q4rdna_plan_set_flags), e.g.
+        CFG_OVERLAP_PREVIOUS: programmatic dependent launch (B = 1..2)."""
+        check(_lib().q4rdna_plan_set_flags(self._h, flags), "plan_set_flags")
+
     def set_segments(self, segments: int):
         """run() as `segments` overlapping launches (q4rdna_plan_set_segments;
         1 or 0 = one launch, the default)."""
@@ -492,6 +498,6 @@ def report_stats() -> None:
 
 
 def kernel_name(B: int = 1) -> str:
-    """Name of the GEMV kernel the library launches for batch B: the int8
-    tensor-core batch-1 kernel for B = 1..2, the int8 tile path for B = 3..16."""
-    return "q4::q4_gemv_mb_kernel" if B >= 3 else "q4::q4_gemv_i8_kernel"
+    """Name of the GEMV kernel the library launches for batch B: the CTA-split
+    int8 kernel for B = 1..2, the int8 tile path for B = 3..16."""
+    return "q4::q4_gemv_mb_kernel" if B >= 3 else "q4::q4_gemv_cta_kernel"
