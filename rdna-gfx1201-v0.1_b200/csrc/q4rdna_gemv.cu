@@ -32,6 +32,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 #include <new>
 #include <vector>
 
@@ -63,6 +64,12 @@ struct Task {
     int pad2;
     float *nss;         // fused RMSNorm with S > 1: sums of h^2 per [RB][S][B]
     float *mirror[kMaxMirrors];  // [B][N] each, on this GPU or a peer (plain P2P stores)
+    // tensor-core tile path (B >= kTcMinBatch, q4rdna_gemv_tc.cuh)
+    uint8_t *img;       // the prepared activation: one operand image per chunk of 4 groups
+    float *csum;        // fused RMSNorm: sum of h^2 per [chunk][BP]
+    long long chunk_begin;  // first prep-kernel CTA of this task
+    int rbi;            // row blocks per work item (2 on the tile path without SwiGLU, else 1)
+    int pad3;
 };
 
 struct Launch {
@@ -71,6 +78,7 @@ struct Launch {
     int ntasks;
     int B;
     long long total_items;
+    long long total_chunks;  // tensor-core tile path: prep-kernel CTAs
 };
 
 // ---------------------------------------------------------------- device helpers
@@ -158,11 +166,13 @@ __device__ unsigned int g_fault;
 #include "q4rdna_gemv_i8.cuh"
 #include "q4rdna_gemv_cta.cuh"
 #include "q4rdna_gemv_mb.cuh"
+#include "q4rdna_gemv_tc.cuh"
 
 // ------------------------------------------------------------------ host side
 
 constexpr int kMaxDevices = 64;
 constexpr int kTileMinBatch = 3;  // B >= 3 runs on the tile path (q4rdna_gemv_mb.cuh)
+constexpr int kTcMinBatch = 8;    // B >= 8: the tensor-core tile path (q4rdna_gemv_tc.cuh)
 std::atomic<uint64_t> g_launches{0};
 
 struct KernelCfg {
@@ -257,9 +267,29 @@ Split make_split(int G, int requested) {
     return Split{(G + Gs - 1) / Gs, Gs};
 }
 
-// CTAs resident at once: the CTA-split kernel (B = 1..2) or the tile path.
+// Tensor-core tile path: K-ranges of whole chunks (Gs a multiple of kTcCG), so
+// that every range starts at a chunk of the prepared activation.
+int tc_chunks(int G) { return (G + kTcCG - 1) / kTcCG; }
+Split make_split_tc(int G, int requested) {
+    const int nch = tc_chunks(G);
+    requested = std::max(1, std::min(requested, nch));
+    const int Gs = (nch + requested - 1) / requested * kTcCG;
+    return Split{(G + Gs - 1) / Gs, Gs};
+}
+Split split_of(int G, int requested, int B) {
+    return B >= kTcMinBatch ? make_split_tc(G, requested) : make_split(G, requested);
+}
+
+// Row blocks per work item: two on the tensor-core tile path (one with SwiGLU,
+// whose up and gate tiles fill the item's two A-blocks), else one.
+int rows_per_item(int B, int op) { return B >= kTcMinBatch && op != Q4RDNA_OP_SWIGLU ? 2 : 1; }
+long long task_items(const Task &T) { return (long long)((T.RB + T.rbi - 1) / T.rbi) * T.S; }
+
+// CTAs resident at once: the CTA-split kernel (B = 1..2), the tensor-core
+// tile path (one CTA per SM) or the mma.sync tile path.
 long long resident_ctas(int pb, bool dual, const DeviceInfo &d) {
     if (pb < kTileMinBatch) return (long long)d.sms * d.occ_cta[pb - 1][dual];
+    if (pb >= kTcMinBatch) return d.sms;
     return (long long)d.sms * d.occ_tile[tile_class(pb)][dual];
 }
 
@@ -286,16 +316,23 @@ int select_split_for(int N, int K, int B, int op, const DeviceInfo &d) {
     const bool dual = op == Q4RDNA_OP_SWIGLU;
     const long long ctas = resident_ctas(B, dual, d);
     if (B < kTileMinBatch) return make_split(G, cta_split(RB, G, ctas)).S;
+    if (B >= kTcMinBatch) {  // about one item per SM
+        const long long items = (RB + rows_per_item(B, op) - 1) / rows_per_item(B, op);
+        return make_split_tc(G, (int)std::min<long long>((ctas + items - 1) / items, G)).S;
+    }
     const long long S = (ctas + RB - 1) / RB;
     return make_split(G, (int)std::min<long long>(S, G)).S;
 }
 
-int resolve_split(int N, int K, int B, int op, const q4rdna_cfg *cfg, const DeviceInfo &d) {
+Split resolve(int N, int K, int B, int op, const q4rdna_cfg *cfg, const DeviceInfo &d) {
     const int G = K / Q4_GROUP;
     int req = cfg != nullptr && cfg->split > 0 ? cfg->split : env_split();
     if (req <= 0) req = select_split_for(N, K, B, op, d);
     if (N > (int)(65536 / sizeof(unsigned)) * Q4_BLOCK_ROWS) req = 1;
-    return make_split(G, req).S;
+    return split_of(G, req, B);
+}
+int resolve_split(int N, int K, int B, int op, const q4rdna_cfg *cfg, const DeviceInfo &d) {
+    return resolve(N, K, B, op, cfg, d).S;
 }
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -317,19 +354,42 @@ size_t sumsq_bytes(int N, int B, int S) {
     return (size_t)RB * S * B * sizeof(float);
 }
 
+// Tensor-core tile path: the prepared activation of one task (operand images
+// of every chunk, then the RMSNorm chunk sums when `norm`).
+int tc_bp(int pb) { return pb <= 8 ? 8 : 16; }
+size_t tc_img_bytes(int K, int pb) {
+    return align256((size_t)tc_chunks(K / Q4_GROUP) * (tc_bp(pb) == 8 ? Tc<8>::CHUNK : Tc<16>::CHUNK));
+}
+size_t tc_prep_bytes(int K, int pb, bool norm) {
+    return tc_img_bytes(K, pb) + (norm ? align256((size_t)tc_chunks(K / Q4_GROUP) * tc_bp(pb) * sizeof(float)) : 0);
+}
+
 // Workspace of one q4rdna_gemv* call: ticket area + partials + the RMSNorm sums
-// (reserved for every call, so one size query serves both; 0 when S == 1).
-size_t ws_bytes_for(int N, int B, int S, int op) {
+// (reserved for every call, so one size query serves both; nothing when S == 1),
+// then, on the tensor-core tile path, the prepared activation -- after the
+// ticket area even when S == 1, so that no call writes over the tickets.
+size_t ws_split_bytes(int N, int B, int S, int op) {
     return S <= 1 ? 0 : kTicketArea + partial_bytes(N, B, S, op) + sumsq_bytes(N, B, S);
+}
+size_t ws_prep_offset(int N, int B, int S, int op) {
+    return align256(S <= 1 ? kTicketArea : ws_split_bytes(N, B, S, op));
+}
+size_t ws_bytes_for(int N, int K, int B, int S, int op) {
+    if (B < kTcMinBatch) return ws_split_bytes(N, B, S, op);
+    return ws_prep_offset(N, B, S, op) + tc_prep_bytes(K, B, true);
 }
 
 // Workspace of one plan task: its own tickets + partials (+ RMSNorm sums), fixed
-// for the plan's life.
-size_t plan_ws_bytes_for(int N, int B, int S, int op, bool norm) {
+// for the plan's life; on the tensor-core tile path the prepared activation
+// follows.
+size_t plan_split_bytes(int N, int B, int S, int op, bool norm) {
     if (S <= 1) return 0;
     const int RB = (N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
     return align256((size_t)RB * sizeof(unsigned)) + align256(partial_bytes(N, B, S, op)) +
            (norm ? align256(sumsq_bytes(N, B, S)) : 0);
+}
+size_t plan_ws_bytes_for(int N, int K, int B, int S, int op, bool norm) {
+    return plan_split_bytes(N, B, S, op, norm) + (B >= kTcMinBatch ? tc_prep_bytes(K, B, norm) : 0);
 }
 
 // Work items per resident CTA that a tile-path plan's split-K choice aims at
@@ -385,6 +445,69 @@ q4rdna_status launch_cta(const Launch &L, int pb, bool dual, bool norm, cudaStre
     return Q4RDNA_OK;
 }
 
+// The tensor-core tile path: q4_tc_prep_kernel over L's chunks, then the
+// persistent q4_tc_gemv_kernel (one CTA per SM), launched as a programmatic
+// dependent of the prep kernel so that its weight copies start while the prep
+// kernel finishes.  overlap: the prep kernel is itself a programmatic
+// dependent of the previous kernel of the stream.
+template <int BP>
+const void *tc_gemv_fn(bool dual) {
+    return dual ? (const void *)q4_tc_gemv_kernel<BP, true> : (const void *)q4_tc_gemv_kernel<BP, false>;
+}
+
+bool tc_attributes() {
+    static std::mutex mu;
+    static bool done[kMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return false;
+    std::lock_guard<std::mutex> lock(mu);
+    if (done[dev]) return true;
+    for (int dual = 0; dual < 2; ++dual) {
+        if (cudaFuncSetAttribute(tc_gemv_fn<8>(dual != 0), cudaFuncAttributeMaxDynamicSharedMemorySize, Tc<8>::SMEM) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(tc_gemv_fn<16>(dual != 0), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 Tc<16>::SMEM) != cudaSuccess)
+            return false;
+    }
+    done[dev] = true;
+    return true;
+}
+
+q4rdna_status launch_tc(const Launch &L, int pb, bool dual, cudaStream_t stream, bool overlap = false) {
+    DeviceInfo d;
+    if (!device_info(d)) return Q4RDNA_ERR_DEVICE;
+    if (!tc_attributes()) return Q4RDNA_ERR_CUDA;
+    if (L.total_items <= 0 || L.total_chunks <= 0) return Q4RDNA_ERR_INVALID_ARGUMENT;
+    const int bp = tc_bp(pb);
+    Launch arg = L;
+    void *args[] = {&arg};
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t pc = {};
+    pc.gridDim = dim3((unsigned)L.total_chunks);
+    pc.blockDim = dim3(128);
+    pc.stream = stream;
+    if (overlap) {
+        pc.attrs = at;
+        pc.numAttrs = 1;
+    }
+    const void *prep = bp == 8 ? (const void *)q4_tc_prep_kernel<8> : (const void *)q4_tc_prep_kernel<16>;
+    if (cudaLaunchKernelExC(&pc, prep, args) != cudaSuccess) return Q4RDNA_ERR_CUDA;
+    cudaLaunchConfig_t mc = {};
+    mc.gridDim = dim3((unsigned)std::min<long long>(L.total_items, d.sms));
+    mc.blockDim = dim3(kTcThreads);
+    mc.dynamicSmemBytes = bp == 8 ? Tc<8>::SMEM : Tc<16>::SMEM;
+    mc.stream = stream;
+    mc.attrs = at;
+    mc.numAttrs = 1;
+    if (cudaLaunchKernelExC(&mc, bp == 8 ? tc_gemv_fn<8>(dual) : tc_gemv_fn<16>(dual), args) != cudaSuccess)
+        return Q4RDNA_ERR_CUDA;
+    if (cudaGetLastError() != cudaSuccess) return Q4RDNA_ERR_CUDA;
+    g_launches.fetch_add(2, std::memory_order_relaxed);
+    return Q4RDNA_OK;
+}
+
 q4rdna_status gemv_common(int op, const uint8_t *w, const uint8_t *w2, const float *x, const float *add, float *y,
                           int N, int K, int B, const q4rdna_cfg *cfg, void *ws, size_t ws_bytes,
                           cudaStream_t stream, const float *gn = nullptr, float eps = 0.0f) {
@@ -400,15 +523,20 @@ q4rdna_status gemv_common(int op, const uint8_t *w, const uint8_t *w2, const flo
     if (!device_info(d)) return Q4RDNA_ERR_DEVICE;
     const int G = K / Q4_GROUP;
     const int RB = (N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
-    Split sp = make_split(G, resolve_split(N, K, B, op, cfg, d));
-    if (N > kMaxSplitRows) sp = make_split(G, 1);  // beyond the ticket area: no split
+    Split sp = resolve(N, K, B, op, cfg, d);
+    if (N > kMaxSplitRows) sp = split_of(G, 1, B);  // beyond the ticket area: no split
+    const bool tc = B >= kTcMinBatch;
     unsigned *ticket = nullptr;
     float *part = nullptr;
-    if (sp.S > 1) {
-        const size_t need = ws_bytes_for(N, B, sp.S, op);
+    uint8_t *prep = nullptr;
+    if (sp.S > 1 || tc) {
+        const size_t need = ws_bytes_for(N, K, B, sp.S, op);
         if (ws == nullptr || ws_bytes < need || !aligned(ws, 256)) return Q4RDNA_ERR_WORKSPACE;
-        ticket = static_cast<unsigned *>(ws);
-        part = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + kTicketArea);
+        if (sp.S > 1) {
+            ticket = static_cast<unsigned *>(ws);
+            part = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + kTicketArea);
+        }
+        if (tc) prep = static_cast<uint8_t *>(ws) + ws_prep_offset(N, B, sp.S, op);
     }
     // One launch for the whole batch: B < tile_min_batch() on the batch-1 kernels, the rest
     // on the tile path; the weights are streamed once.
@@ -429,8 +557,15 @@ q4rdna_status gemv_common(int op, const uint8_t *w, const uint8_t *w2, const flo
     T.gn = gn;
     T.eps = eps;
     T.nss = (gn != nullptr && sp.S > 1) ? part + partial_bytes(N, B, sp.S, op) / sizeof(float) : nullptr;
-    L.total_items = (long long)RB * sp.S;
+    T.rbi = rows_per_item(B, op);
+    T.chunk_begin = 0;
+    T.img = prep;
+    T.csum = (tc && gn != nullptr) ? reinterpret_cast<float *>(prep + tc_img_bytes(K, B)) : nullptr;
+    L.total_items = task_items(T);
+    L.total_chunks = tc_chunks(G);
     const bool dual = op == Q4RDNA_OP_SWIGLU;
+    if (tc)
+        return launch_tc(L, B, dual, stream, cfg != nullptr && (cfg->flags & Q4RDNA_CFG_OVERLAP_PREVIOUS));
     if (B < kTileMinBatch)  // one CTA per (row block, K-range) (q4rdna_gemv_cta.cuh)
         return launch_cta(L, B, dual, gn != nullptr, stream,
                           cfg != nullptr && (cfg->flags & Q4RDNA_CFG_OVERLAP_PREVIOUS));
@@ -552,10 +687,12 @@ Task *upload_tasks(std::vector<Task> t) {
         const long long cb = (long long)b.Gs * (b.op == Q4RDNA_OP_SWIGLU ? 2 : 1);
         return ca > cb;
     });
-    long long items = 0;
+    long long items = 0, chunks = 0;
     for (Task &T : t) {
         T.item_begin = items;
-        items += (long long)T.RB * T.S;
+        items += task_items(T);
+        T.chunk_begin = chunks;
+        chunks += tc_chunks(T.G);
     }
     Task *d = nullptr;
     if (cudaMalloc(&d, sizeof(Task) * t.size()) != cudaSuccess) return nullptr;
@@ -572,6 +709,8 @@ struct q4rdna_plan {
     bool dual = false;  // the plan holds a SwiGLU task
     bool norm = false;  // the plan holds a fused-RMSNorm task
     bool cta = false;   // B = 1..2: the CTA-split kernel (one CTA per item), else the tile path
+    bool tc = false;    // B >= kTcMinBatch: the tensor-core tile path (prep kernel + GEMV kernel)
+    long long chunks = 0;  // tensor-core tile path: chunks of all tasks (prep-kernel CTAs)
     bool overlap = false;  // q4rdna_plan_set_flags(Q4RDNA_CFG_OVERLAP_PREVIOUS): programmatic dependent launch
     long long items = 0;
     Task *table = nullptr;     // device
@@ -582,7 +721,7 @@ struct q4rdna_plan {
     // q4rdna_plan_run_host: consecutive task ranges with their own device tables
     struct Segment {
         int first = 0, count = 0;
-        long long items = 0;
+        long long items = 0, chunks = 0;
         int grid = 1;
         Task *table = nullptr;  // item_begin rebased to the segment
         Task *gtable[2] = {nullptr, nullptr};  // the same with the gather's mirrors, per gathered buffer
@@ -625,6 +764,7 @@ namespace {
 // One launch of (a segment of) a plan on its kernel.
 q4rdna_status plan_launch(const q4rdna_plan *plan, const Launch &L, int grid, cudaStream_t stream) {
     if (plan->cta) return launch_cta(L, plan->nb, plan->dual, plan->norm, stream, plan->overlap);
+    if (plan->tc) return launch_tc(L, plan->nb, plan->dual, stream, plan->overlap);
     return launch(L, grid, plan->nb, plan->dual, stream, plan->norm);
 }
 
@@ -667,7 +807,7 @@ size_t q4rdna_workspace_bytes(int N, int K, int B, int op, const q4rdna_cfg *cfg
     if (check_shape(N, K, B) != Q4RDNA_OK) return 0;
     DeviceInfo d;
     if (!device_info(d)) return 0;
-    return ws_bytes_for(N, B, resolve_split(N, K, B, op, cfg, d), op);
+    return ws_bytes_for(N, K, B, resolve_split(N, K, B, op, cfg, d), op);
 }
 
 q4rdna_status q4rdna_workspace_init(void *workspace, size_t bytes, q4rdna_stream_t stream) {
@@ -727,7 +867,7 @@ q4rdna_status plan_create_rdna(const q4rdna_gemv_desc *descs, int count, int B, 
     std::vector<Task> host(count);
     std::vector<size_t> ws_off(count);
     size_t ws_total = 0;
-    long long items = 0;
+    long long items = 0, chunks = 0;
     uint64_t wbytes = 0, abytes = 0;
     // Split-K only as far as the whole plan needs it.  B = 1..2 (the CTA-split
     // kernel, one CTA per (row block, K-range)): as many K-ranges per tensor as
@@ -742,9 +882,13 @@ q4rdna_status plan_create_rdna(const q4rdna_gemv_desc *descs, int count, int B, 
         any_dual_task = any_dual_task || descs[i].op == Q4RDNA_OP_SWIGLU;
     }
     const bool cta = B < kTileMinBatch;
+    const bool tc = B >= kTcMinBatch;
     const long long ctas = resident_ctas(B, any_dual_task, d);
     const double want_items = kPlanItemsPerWorker * (double)ctas;
-    const int tile_split = total_rb > 0 ? (int)std::max(1.0, std::ceil(want_items / (double)total_rb)) : 1;
+    // the tensor-core path's items hold two row blocks (one with SwiGLU)
+    const double item_rb = tc ? 2.0 : 1.0;
+    const int tile_split =
+        total_rb > 0 ? (int)std::max(1.0, std::ceil(want_items * item_rb / (double)total_rb)) : 1;
     for (int i = 0; i < count; ++i) {
         const q4rdna_gemv_desc &e = descs[i];
         q4rdna_status st = check_shape(e.N, e.K, B);
@@ -760,7 +904,7 @@ q4rdna_status plan_create_rdna(const q4rdna_gemv_desc *descs, int count, int B, 
         const int G = e.K / Q4_GROUP;
         const int RB = (e.N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
         const int req = e.split > 0 ? e.split : cta ? cta_split(total_rb, G, ctas) : std::min(tile_split, G);
-        const Split sp = make_split(G, req);
+        const Split sp = split_of(G, req, B);
         Task &T = host[i];
         T.w = e.tiles; T.w2 = e.gate_tiles; T.x = e.x; T.add = e.add; T.y = e.y;
         T.part = nullptr; T.ticket = nullptr;
@@ -768,9 +912,14 @@ q4rdna_status plan_create_rdna(const q4rdna_gemv_desc *descs, int count, int B, 
         T.item_begin = items;
         T.gn = e.norm_weight;
         T.eps = e.norm_eps;
-        items += (long long)RB * sp.S;
+        T.rbi = rows_per_item(B, e.op);
+        T.chunk_begin = chunks;
+        T.img = nullptr;
+        T.csum = nullptr;
+        items += task_items(T);
+        chunks += tc_chunks(G);
         ws_off[i] = ws_total;
-        ws_total += plan_ws_bytes_for(e.N, B, sp.S, e.op, e.norm_weight != nullptr);
+        ws_total += plan_ws_bytes_for(e.N, e.K, B, sp.S, e.op, e.norm_weight != nullptr);
         wbytes += (uint64_t)planes * Q4_TENSOR_BYTES(e.N, e.K);
         abytes += (uint64_t)planes * Q4_TENSOR_BYTES(e.N, e.K) + 4ull * e.K * B + 4ull * e.N * B +
                   (e.op == Q4RDNA_OP_ADD ? 4ull * e.N * B : 0ull);
@@ -782,6 +931,12 @@ q4rdna_status plan_create_rdna(const q4rdna_gemv_desc *descs, int count, int B, 
     if (ws_total > 0 && cudaMemset(p->workspace, 0, ws_total) != cudaSuccess) { q4rdna_plan_destroy(p); return Q4RDNA_ERR_CUDA; }
     for (int i = 0; i < count; ++i) {
         Task &T = host[i];
+        if (tc) {  // the prepared activation follows the split workspace
+            uint8_t *prep = static_cast<uint8_t *>(p->workspace) + ws_off[i] +
+                            plan_split_bytes(T.N, B, T.S, T.op, T.gn != nullptr);
+            T.img = prep;
+            if (T.gn != nullptr) T.csum = reinterpret_cast<float *>(prep + tc_img_bytes(T.K, B));
+        }
         if (T.S > 1) {
             uint8_t *base = static_cast<uint8_t *>(p->workspace) + ws_off[i];
             T.ticket = reinterpret_cast<unsigned *>(base);
@@ -801,6 +956,8 @@ q4rdna_status plan_create_rdna(const q4rdna_gemv_desc *descs, int count, int B, 
     for (int i = 0; i < count; ++i) p->norm = p->norm || descs[i].norm_weight != nullptr;
     p->host = host;
     p->cta = cta;
+    p->tc = tc;
+    p->chunks = chunks;
     p->grid = cta ? (int)std::min<long long>(items, INT32_MAX) : grid_for(items, B, any_dual, d);
     p->ws_bytes = ws_total; p->weight_bytes = wbytes; p->algo_bytes = abytes;
     *out = p;
@@ -905,6 +1062,7 @@ q4rdna_status q4rdna_plan_run(q4rdna_plan *plan, q4rdna_stream_t stream) {
             L.ntasks = plan->count;
             L.B = plan->B;
             L.total_items = plan->items;
+            L.total_chunks = plan->chunks;
             st = plan_launch(plan, L, plan->grid, (cudaStream_t)stream);
         }
         if (st != Q4RDNA_OK) return st;
@@ -920,6 +1078,7 @@ q4rdna_status q4rdna_plan_run(q4rdna_plan *plan, q4rdna_stream_t stream) {
         L.ntasks = plan->count;
         L.B = plan->B;
         L.total_items = plan->items;
+        L.total_chunks = plan->chunks;
         st = plan_launch(plan, L, plan->grid, (cudaStream_t)stream);
     }
     if (st != Q4RDNA_OK) return st;
@@ -1051,6 +1210,7 @@ q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t
         }
         const long long end = last < n ? p->host[last].item_begin : p->items;
         sg.items = end - base;
+        for (const Task &T : t) sg.chunks += tc_chunks(T.G);
         sg.grid = grid_for(sg.items, p->B, p->dual, d);
         p->segs.push_back(sg);  // owned by the plan from here on (freed on failure paths below)
         q4rdna_plan::Segment &g = p->segs.back();
@@ -1136,6 +1296,7 @@ q4rdna_status launch_segments(q4rdna_plan *plan, cudaStream_t cs, const uint8_t 
         L.ntasks = sg.count;
         L.B = plan->B;
         L.total_items = sg.items;
+        L.total_chunks = sg.chunks;
         const q4rdna_status st = plan_launch(plan, L, sg.grid, c);
         if (st != Q4RDNA_OK) return st;
         if (cudaEventRecord(sg.y_ready, c) != cudaSuccess) return Q4RDNA_ERR_CUDA;
