@@ -78,7 +78,8 @@ constexpr int kTcSlots = 4;                              // TMEM accumulator slo
 // warp roles: 0 copies, 1..3 MMA issue, 4..7 unpack, 8..23 epilogue (A-block x
 // half of the batch columns x TMEM lane quarter).  24 warps, six per SM
 // sub-partition (80 registers per thread).
-constexpr int kTcMmaWarp0 = 1, kTcMmaWarps = 3, kTcUnpackWarp0 = 4, kTcEpiWarp0 = 8, kTcEpiWarps = 16;
+constexpr int kTcMmaWarp0 = 1, kTcMmaWarps = 3, kTcUnpackWarp0 = 4, kTcUnpackWarps = 4, kTcEpiWarp0 = 8,
+              kTcEpiWarps = 16;
 constexpr int kTcWarps = 24;
 constexpr int kTcThreads = kTcWarps * 32;
 constexpr uint32_t kTcBias = 0x4B400000u;                // f32 1.5 * 2^23
@@ -99,7 +100,7 @@ struct Tc {
     static constexpr int OFF_A = NRAW * RAW;
     static constexpr int OFF_X = OFF_A + NA * kTcAStage;  // SwiGLU gate sums [BP][128]
     static constexpr int OFF_BAR = OFF_X + BP * Q4_BLOCK_ROWS * 4;
-    static constexpr int NBAR = 2 * NRAW + NA + 2 * kTcSlots + kTcMmaWarps + 1;
+    static constexpr int NBAR = 2 * NRAW + NA + 2 * kTcSlots + 2 * kTcMmaWarps + 1;
     static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // TMEM address, last-CTA flag, norm scales
     static constexpr int SMEM = OFF_MISC + 16 + BP * 4;
     // instruction descriptor: D s32, A and B s8, both MN-major, N = NCOL, M = 128
@@ -324,15 +325,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_tc_gemv_kernel(const __grid_
     float *xch = reinterpret_cast<float *>(smem + S::OFF_X);
     const uint32_t bar0 = smem_u32(smem + S::OFF_BAR);
     // mbarriers (8 bytes each).  Group n of the CTA's sequence uses A stage
-    // n % NA and TMEM slot n % NSL; its MMAs are issued by MMA warp n % 3 (a
+    // n % NA and TMEM slot n % NSL; its MMAs are issued by MMA warp n % kTcMmaWarps (a
     // tcgen05.mma or commit holds its issuing thread for about a hundred
     // cycles, so one thread cannot keep up with the stream),
     // whose one commit per group (mma_done) tells the epilogue that the slot
     // holds the sums and the unpack warps that the A stage may be rewritten;
-    // the warp of a chunk's last group also commits to the chunk's raw_empty
-    // (the operand image has been read).  A waiter never falls two phases
-    // behind a barrier: the next phase of each barrier it waits on needs the
-    // waiter's own progress first.
+    // each group's warp also commits to its chunk's raw_empty (the chunk's
+    // operand image has been read).  A waiter never falls two phases behind a
+    // barrier: the next phase of each barrier it waits on needs the waiter's
+    // own progress first.
     auto raw_full = [&](int s) { return bar0 + 8u * s; };                        // copies landed
     auto raw_empty = [&](int s) { return bar0 + 8u * (NRAW + s); };              // unpacked, image read
     auto a_full = [&](int s) { return bar0 + 8u * (2 * NRAW + s); };             // A stage unpacked
@@ -340,6 +341,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_tc_gemv_kernel(const __grid_
     auto acc_empty = [&](int s) { return bar0 + 8u * (2 * NRAW + NA + NSL + s); };  // slot read
     auto drain = [&](int s) { return bar0 + 8u * (2 * NRAW + NA + 2 * NSL + s); };    // issuer s's last MMAs
     const uint32_t epi_bar = bar0 + 8u * (2 * NRAW + NA + 2 * NSL + kTcMmaWarps);  // the epilogue warps meet here
+    // the MMA warps take their waits in group order: group n's warp starts its
+    // waits once group n - 1's warp has passed its own (phase n / kTcMmaWarps of
+    // turn(n % kTcMmaWarps)), so that no waiter is ever a phase ahead of a barrier;
+    // the MMAs themselves overlap
+    auto turn = [&](int j) { return bar0 + 8u * (2 * NRAW + NA + 2 * NSL + kTcMmaWarps + 1 + j); };
     // the completion of group n's MMAs is phase n / NSL of mma_done(n % NSL)
     auto wait_group = [&](uint32_t n) { return mbar_wait(mma_done(n % NSL), (n / NSL) & 1u); };
     uint32_t *misc = reinterpret_cast<uint32_t *>(smem + S::OFF_MISC);  // [0] TMEM address, [1] last-CTA flag
@@ -355,14 +361,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_tc_gemv_kernel(const __grid_
     if (threadIdx.x == 32) {
         for (int s = 0; s < NRAW; ++s) {
             mbar_init(raw_full(s), 1);
-            mbar_init(raw_empty(s), 4 + 1);  // unpack warps, the commit of the last group's MMAs
+            mbar_init(raw_empty(s), kTcUnpackWarps + kTcCG);  // unpack warps, one commit per group
         }
-        for (int s = 0; s < NA; ++s) mbar_init(a_full(s), 4);
+        for (int s = 0; s < NA; ++s) mbar_init(a_full(s), kTcUnpackWarps);
         for (int s = 0; s < NSL; ++s) {
             mbar_init(mma_done(s), 1);
             mbar_init(acc_empty(s), kTcEpiWarps);
         }
-        for (int s = 0; s < kTcMmaWarps; ++s) mbar_init(drain(s), 1);
+        for (int s = 0; s < kTcMmaWarps; ++s) {
+            mbar_init(drain(s), 1);
+            mbar_init(turn(s), 1);
+        }
+        mbar_arrive(turn(0));  // group 0 has no predecessor
         mbar_init(epi_bar, kTcEpiWarps);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -429,7 +439,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_tc_gemv_kernel(const __grid_
                 mbar_wait(raw_full(k % NRAW), (k / NRAW) & 1u);
         }
     } else if (warp < kTcUnpackWarp0) {
-        // ---------------------------------------------------------- MMA issue (warp 1 + j: groups n % 3 == j)
+        // ---------------------------------------------------------- MMA issue (warp 1 + j: groups n % kTcMmaWarps == j)
         const int j = warp - kTcMmaWarp0;
         if (lane == 0) {
             uint32_t rit = 0, ait = 0;
@@ -439,18 +449,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_tc_gemv_kernel(const __grid_
                 for (int g = I.g0; ok && g < I.g1; g += kTcCG, ++rit) {
                     const int ng = min(kTcCG, I.g1 - g);
                     const int s = rit % NRAW;
-                    bool have = false;  // does this chunk hold one of this warp's groups?
-                    for (int gi = 0; gi < ng; ++gi) have = have || (int)((ait + gi) % kTcMmaWarps) == j;
-                    if (have && !mbar_wait(raw_full(s), (rit / NRAW) & 1u)) { ok = false; break; }
                     const uint32_t img = smem_u32(raw + (size_t)s * S::RAW + kTcRawW);
                     for (int gi = 0; gi < ng; ++gi, ++ait) {
                         if ((int)(ait % kTcMmaWarps) != j) continue;
                         const int as = ait % NA, ts = ait % NSL;
-                        if (!mbar_wait(a_full(as), (ait / NA) & 1u) ||
+                        if (!mbar_wait(turn(j), (ait / kTcMmaWarps) & 1u) || !mbar_wait(raw_full(s), (rit / NRAW) & 1u) ||
+                            !mbar_wait(a_full(as), (ait / NA) & 1u) ||
                             !mbar_wait(acc_empty(ts), ((ait / NSL) & 1u) ^ 1u)) {
                             ok = false;
                             break;
                         }
+                        mbar_arrive(turn((j + 1) % kTcMmaWarps));  // group ait + 1's warp may wait now
                         tc_fence_after();
                         const uint32_t A = smem_u32(abuf + (size_t)as * kTcAStage);
                         for (int a = 0; a < I.nab; ++a) {
@@ -460,7 +469,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_tc_gemv_kernel(const __grid_
                                           smem_desc(img + gi * S::IMG + p * S::IMGP, 128, 512), S::IDESC);
                         }
                         tc_commit(mma_done(ts));
-                        if (gi == ng - 1) tc_commit(raw_empty(s));  // the chunk's image has been read
+                        // this group's MMAs have read the chunk's image (a commit covers only
+                        // the committing thread's MMAs; in a short last chunk the last group
+                        // stands in for the missing ones)
+                        for (int c = (gi == ng - 1 ? kTcCG - ng : 0); c >= 0; --c) tc_commit(raw_empty(s));
                         issued = true;
                     }
                 }
