@@ -81,9 +81,12 @@ const char *q4rdna_version(void);
 int q4rdna_select_split(int N, int K, int B, int op);
 
 /* Device workspace a single GEMV needs: split-K partial sums plus arrival
- * tickets.  0 when the chosen split is 1.  A workspace must be zero-filled once
- * when it is allocated (q4rdna_workspace_init); every call leaves it zeroed
- * again.  Calls that share a workspace must be ordered on one stream. */
+ * tickets (0 when the chosen split is 1 and B < 8), and at B >= 8 (the
+ * tensor-core tile path) also the activation prepared for the tensor cores
+ * (4 bytes per element of x, plus a small per-chunk table).  A workspace must
+ * be zero-filled once when it is allocated (q4rdna_workspace_init); every call
+ * leaves its tickets zeroed again.  Calls that share a workspace must be
+ * ordered on one stream. */
 size_t q4rdna_workspace_bytes(int N, int K, int B, int op, const q4rdna_cfg *cfg);
 q4rdna_status q4rdna_workspace_init(void *workspace, size_t bytes, q4rdna_stream_t stream);
 
@@ -363,9 +366,12 @@ uint64_t q4rdna_registry_hits(const char *weight_name);
  * (synchronises the device).  Bit 1: a fused gather (q4rdna_plan_set_gather)
  * stopped waiting for a peer's flag (q4rdna_plan_set_gather_timeout), so the
  * gathered buffer of that run is incomplete; the GEMV outputs of this rank
- * (y) are complete.  Bit 0 is no longer set by any kernel.  0 = no fault;
- * 0xffffffff = the flag could not be read.  No reference counterpart (the
- * reference kernels never wait). */
+ * (y) are complete.  Bit 2: a wait inside the tensor-core tile kernel (B >= 8)
+ * ran out (about 1 s) and the kernel stopped; the outputs of that launch are
+ * invalid and the workspaces it used must be re-initialised
+ * (q4rdna_workspace_init) or the plans re-created.  Bit 0 is no longer set by
+ * any kernel.  0 = no fault; 0xffffffff = the flag could not be read.  No
+ * reference counterpart (the reference kernels never wait). */
 uint32_t q4rdna_take_fault(void);
 /* Prints the reference's exit-time summary to stderr (also run at exit once the
  * registry has loaded); LLAMA_Q4_RDNA_TRACE adds per-tensor hit lines. */

@@ -200,15 +200,17 @@ KernelCfg tile_cfg(int pb, bool dual = true, bool norm = false) {
     return norm ? mb_cfg_n<true>(pb, dual) : mb_cfg_n<false>(pb, dual);
 }
 
-// The CTA-split kernel (B = 1..2).
-template <bool NORM>
+// The CTA-split kernel (B = 1..2); cl: the clustered single-call variant.
+template <bool NORM, bool CL>
 const void *cta_kernel_n(int pb, bool dual) {
     if (pb <= 1)
-        return dual ? (const void *)q4_gemv_cta_kernel<1, true, NORM> : (const void *)q4_gemv_cta_kernel<1, false, NORM>;
-    return dual ? (const void *)q4_gemv_cta_kernel<2, true, NORM> : (const void *)q4_gemv_cta_kernel<2, false, NORM>;
+        return dual ? (const void *)q4_gemv_cta_kernel<1, true, NORM, CL>
+                    : (const void *)q4_gemv_cta_kernel<1, false, NORM, CL>;
+    return dual ? (const void *)q4_gemv_cta_kernel<2, true, NORM, CL> : (const void *)q4_gemv_cta_kernel<2, false, NORM, CL>;
 }
-const void *cta_kernel(int pb, bool dual, bool norm) {
-    return norm ? cta_kernel_n<true>(pb, dual) : cta_kernel_n<false>(pb, dual);
+const void *cta_kernel(int pb, bool dual, bool norm, bool cl = false) {
+    if (cl) return norm ? cta_kernel_n<true, true>(pb, dual) : cta_kernel_n<false, true>(pb, dual);
+    return norm ? cta_kernel_n<true, false>(pb, dual) : cta_kernel_n<false, false>(pb, dual);
 }
 
 struct DeviceInfo {
@@ -308,14 +310,55 @@ int cta_split(long long total_rb, int G, long long ctas) {
     return (int)std::max<long long>(S, 1);
 }
 
-// Selector of single calls: the one-wave rule above at B = 1..2; on the tile
-// path (B = 3..16) about one item per resident CTA.
+// Clusters of S CTA-split CTAs (a single call's row blocks) resident at once,
+// from cudaOccupancyMaxActiveClusters; cached per device, batch, SwiGLU and S.
+int active_clusters(int pb, bool dual, int S) {
+    static std::mutex mu;
+    static int cache[kMaxDevices][2][2][kMaxClusterSplit + 1] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices || S < 2 || S > kMaxClusterSplit) return 0;
+    std::lock_guard<std::mutex> lock(mu);
+    int &c = cache[dev][pb > 1][dual][S];
+    if (c == 0) {
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = dim3((unsigned)S * 64);
+        lc.blockDim = dim3(kThreads);
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = (unsigned)S;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        lc.attrs = at;
+        lc.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, cta_kernel(pb, dual, false, true), &lc) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+        c = std::max(n, -1);  // -1: no cluster of this size fits
+        if (c == 0) c = -1;
+    }
+    return std::max(c, 0);
+}
+
+// Selector of single calls at B = 1..2: the one-wave rule above with at most
+// kMaxClusterSplit K-ranges, so that the call runs as clusters (one per row
+// block), lowered until all the row blocks' clusters are resident at once.
+// Measured on B200 (bench.py --single --single-sweep, us per call): 12288x4096
+// runs 9.4 us at S = 2 and 13.2 us at S = 3, where 96 clusters of 3 no longer
+// fit in one wave; on the tile path (B = 3..16) about one item per resident CTA.
 int select_split_for(int N, int K, int B, int op, const DeviceInfo &d) {
     const int G = K / Q4_GROUP;
     const int RB = (N + Q4_BLOCK_ROWS - 1) / Q4_BLOCK_ROWS;
     const bool dual = op == Q4RDNA_OP_SWIGLU;
     const long long ctas = resident_ctas(B, dual, d);
-    if (B < kTileMinBatch) return make_split(G, cta_split(RB, G, ctas)).S;
+    if (B < kTileMinBatch) {
+        for (int req = std::min(cta_split(RB, G, ctas), kMaxClusterSplit); req > 1; --req) {
+            const int S = make_split(G, req).S;
+            if (S > 1 && S <= kMaxClusterSplit && RB <= active_clusters(B, dual, S)) return S;
+        }
+        return 1;
+    }
     if (B >= kTcMinBatch) {  // about one item per SM
         const long long items = (RB + rows_per_item(B, op) - 1) / rows_per_item(B, op);
         return make_split_tc(G, (int)std::min<long long>((ctas + items - 1) / items, G)).S;
@@ -432,14 +475,25 @@ q4rdna_status launch_cta(const Launch &L, int pb, bool dual, bool norm, cudaStre
     lc.gridDim = dim3((unsigned)L.total_items);
     lc.blockDim = dim3(kThreads);
     lc.stream = stream;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
+    int na = 0;
     if (overlap) {
-        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        at[0].val.programmaticStreamSerializationAllowed = 1;
-        lc.attrs = at;
-        lc.numAttrs = 1;
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
     }
-    if (cudaLaunchKernelExC(&lc, cta_kernel(pb, dual, norm), args) != cudaSuccess) return Q4RDNA_ERR_CUDA;
+    // a single call with 2..8 K-ranges: one cluster of S CTAs per row block
+    const bool cl = L.table == nullptr && L.one.S > 1 && L.one.S <= kMaxClusterSplit;
+    if (cl) {
+        at[na].id = cudaLaunchAttributeClusterDimension;
+        at[na].val.clusterDim.x = (unsigned)L.one.S;
+        at[na].val.clusterDim.y = 1;
+        at[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    lc.attrs = na > 0 ? at : nullptr;
+    lc.numAttrs = na;
+    if (cudaLaunchKernelExC(&lc, cta_kernel(pb, dual, norm, cl), args) != cudaSuccess) return Q4RDNA_ERR_CUDA;
     if (cudaGetLastError() != cudaSuccess) return Q4RDNA_ERR_CUDA;
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return Q4RDNA_OK;
@@ -650,6 +704,13 @@ double host_growth() {
     }();
     return v;
 }
+
+// Kernels whose output stores suit a mapped host buffer: the CTA-split kernel
+// (B = 1..2) and the tensor-core tile path (B >= 8) store whole 128-byte runs
+// of a row block; the mma.sync tile path (B = 3..7) stores 4-byte scattered
+// values, which cost one PCIe transaction each (e2e 7.3 ms at B = 4 against
+// 1.45 ms on the device), so it keeps the output copies.
+bool direct_batch(int B) { return B < kTileMinBatch || B >= kTcMinBatch; }
 
 // Device address of run_host's output buffer when the whole [yh, yh + yb) is
 // pinned host memory mapped for the device (both ends map, at the same
@@ -1165,7 +1226,7 @@ q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t
     if (!device_info(d)) return Q4RDNA_ERR_DEVICE;
     const int n = p->count;
     want = std::max(1, std::min(want, n));
-    uint8_t *yh_dev = graded && xd != nullptr ? mapped_output(yh, yb) : nullptr;
+    uint8_t *yh_dev = graded && xd != nullptr && direct_batch(p->B) ? mapped_output(yh, yb) : nullptr;
     const bool direct = yh_dev != nullptr;
     uint64_t total = 0;
     for (const Task &T : p->host) total += (uint64_t)T.N * T.K * (T.op == Q4RDNA_OP_SWIGLU ? 2 : 1);
@@ -1341,8 +1402,9 @@ q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *
             return Q4RDNA_ERR_CUDA;
         return Q4RDNA_OK;
     }
-    const int want =
-        segments != 0 ? segments : (mapped_output(y_host, y_bytes) != nullptr ? kHostSegmentsDirect : kHostSegments);
+    const int want = segments != 0 ? segments
+                                   : (direct_batch(plan->B) && mapped_output(y_host, y_bytes) != nullptr ? kHostSegmentsDirect
+                                                                                                          : kHostSegments);
     if (plan->seg_request != std::max(1, std::min(want, plan->count)) || !plan->seg_graded || plan->seg_x != x_dev ||
         plan->seg_y != y_dev || plan->seg_yh != y_host) {
         const q4rdna_status st = build_segments(plan, want, static_cast<const uint8_t *>(x_dev), x_bytes,

@@ -12,7 +12,8 @@
 //   * with S > 1 CTA K-ranges, each CTA stores its partial sums to the
 //     workspace and the last CTA to arrive at the row block (arrival ticket)
 //     adds them in ascending order with all 256 threads and applies the add /
-//     SwiGLU epilogue.
+//     SwiGLU epilogue; a single call with S <= 8 instead runs each row block's
+//     CTAs as one cluster and adds the sums through distributed shared memory.
 // Accumulation order of an output: exact int32 inside a group; the groups of a
 // warp in ascending order, sum = fma(scale / 16, v * 2^e, sum); warps in
 // ascending order; CTA K-ranges in ascending order.  The fused RMSNorm's sum of
@@ -43,17 +44,41 @@ __device__ __forceinline__ void cta_fetch_x(const Task &T, int B, int g, int lan
                       : make_float2(0.0f, 0.0f);
 }
 
+// Single calls with 2..8 K-ranges run each row block's K-range CTAs as one
+// thread-block cluster: the CTAs write their sums into the first CTA's shared
+// memory (distributed shared memory) and meet at one cluster barrier, instead
+// of a round trip through the workspace and an arrival ticket.  The first CTA
+// then adds the K-ranges in ascending order, as the last-arrival path does, so
+// the outputs are the same bits either way.
+constexpr int kMaxClusterSplit = 8;
+
 template <int BB>
 struct CtaSmem {
     I8X<BB> xs[kWarps][2];
     float red[kWarps][2][4][BB][32];  // [warp][plane][q][b][lane]
     float ssq[kWarps][BB];            // fused RMSNorm: each warp's sum of h^2 per batch column
+    float cpart[kMaxClusterSplit][2][4 * BB * 32];  // cluster path, first CTA: [K-range][plane][output]
+    float cssq[kMaxClusterSplit][BB];               // cluster path, first CTA: sums of h^2 per K-range
     unsigned last;
 };
 
+// Stores v into the shared memory of the cluster's CTA 0 at the address that
+// p has in this CTA.
+__device__ __forceinline__ void st_cluster0(const float *p, float v) {
+    uint32_t a = (uint32_t)__cvta_generic_to_shared(p), r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(r) : "r"(a));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(r), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // One CTA item of task T: row block rb, K-range sc.  NORM: the kernel has the
-// fused-RMSNorm path (used by tasks with a norm weight, T.gn != null).
-template <int BB, bool DUAL, bool NORM>
+// fused-RMSNorm path (used by tasks with a norm weight, T.gn != null).  CL: the
+// launch is clustered by row block (K-range sc = cluster rank sc).
+template <int BB, bool DUAL, bool NORM, bool CL>
 __device__ __forceinline__ void cta_item(const Task &T, int B, int rb, int sc, CtaSmem<BB> &sm) {
     constexpr int planes = DUAL ? 2 : 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -194,12 +219,46 @@ __device__ __forceinline__ void cta_item(const Task &T, int B, int rb, int sc, C
                 for (int pl = 0; pl < planes; ++pl) v[pl] *= r;
             }
             put_y(T, idx, finish(v[0], v[planes - 1], T.op, T.add, idx));
+        } else if (CL) {
+#pragma unroll
+            for (int pl = 0; pl < planes; ++pl) st_cluster0(&sm.cpart[sc][pl][o], v[pl]);
         } else {
 #pragma unroll
             for (int pl = 0; pl < planes; ++pl) __stcg(&T.part[(size_t)sc * split_stride + (size_t)pl * B * T.N + idx], v[pl]);
         }
     }
     if (T.S == 1) return;
+
+    if (CL) {
+        // the cluster's CTAs meet once; CTA 0 adds the K-ranges in ascending order
+        if (norm && threadIdx.x < B) st_cluster0(&sm.cssq[sc][threadIdx.x], cta_sumsq(threadIdx.x));
+        cluster_sync_all();
+        if (sc != 0) return;
+        for (int o = threadIdx.x; o < kOut; o += kThreads) {
+            const int ln = o & 31, b = (o >> 5) % BB, q = o / (32 * BB);
+            if (b >= B) continue;
+            const int lt = ln >> 3, lh = (ln >> 2) & 1, lc = ln & 3;
+            const int row = (rb * Q4_BLOCK_TILES + lt) * Q4_TILE_ROWS + 16 * lh + lc + 4 * q;
+            if (row >= T.N) continue;
+            float v[planes];
+#pragma unroll
+            for (int pl = 0; pl < planes; ++pl) {
+                float s = 0.0f;
+                for (int sp = 0; sp < T.S; ++sp) s += sm.cpart[sp][pl][o];
+                v[pl] = s;
+            }
+            if (norm) {  // the K-ranges' sums of h^2 in ascending order
+                float q2 = 0.0f;
+                for (int sp = 0; sp < T.S; ++sp) q2 += sm.cssq[sp][b];
+                const float r = norm_scale(T, q2);
+#pragma unroll
+                for (int pl = 0; pl < planes; ++pl) v[pl] *= r;
+            }
+            const size_t idx = (size_t)b * T.N + row;
+            put_y(T, idx, finish(v[0], v[planes - 1], T.op, T.add, idx));
+        }
+        return;
+    }
 
     // K-ranges of several CTAs: the last one to arrive adds them in order
     if (norm && threadIdx.x < B) __stcg(&T.nss[((size_t)rb * T.S + sc) * B + threadIdx.x], cta_sumsq(threadIdx.x));
@@ -233,8 +292,8 @@ __device__ __forceinline__ void cta_item(const Task &T, int B, int rb, int sc, C
 
 // One CTA per item (not persistent).  HAS_DUAL = false: the launch holds no
 // SwiGLU task; NORM = false: no fused-RMSNorm task; those paths are compiled
-// out.
-template <int BB, bool HAS_DUAL, bool NORM>
+// out.  CL: a single call launched as clusters of S CTAs (one per row block).
+template <int BB, bool HAS_DUAL, bool NORM, bool CL>
 __global__ void __launch_bounds__(kThreads, 2) q4_gemv_cta_kernel(const __grid_constant__ Launch L) {
     __shared__ CtaSmem<BB> sm;
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -243,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 2) q4_gemv_cta_kernel(const __grid_c
     const int local = (int)(it - T.item_begin);
     const int rb = local / T.S, sc = local % T.S;
     if (HAS_DUAL && T.op == Q4RDNA_OP_SWIGLU)
-        cta_item<BB, true, NORM>(T, L.B, rb, sc, sm);
+        cta_item<BB, true, NORM, CL>(T, L.B, rb, sc, sm);
     else
-        cta_item<BB, false, NORM>(T, L.B, rb, sc, sm);
+        cta_item<BB, false, NORM, CL>(T, L.B, rb, sc, sm);
 }

@@ -499,5 +499,8 @@ def report_stats() -> None:
 
 def kernel_name(B: int = 1) -> str:
     """Name of the GEMV kernel the library launches for batch B: the CTA-split
-    int8 kernel for B = 1..2, the int8 tile path for B = 3..16."""
+    int8 kernel for B = 1..2, the mma.sync tile path for B = 3..7, the tcgen05
+    tile path (after its activation-prep kernel) for B = 8..16."""
+    if B >= 8:
+        return "q4::q4_tc_gemv_kernel (+ q4::q4_tc_prep_kernel)"
     return "q4::q4_gemv_mb_kernel" if B >= 3 else "q4::q4_gemv_cta_kernel"

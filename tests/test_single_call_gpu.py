@@ -105,3 +105,50 @@ def test_single_call_ops_with_overlap(cuda, N, K, op):
             g64, mg = oracle.gemv_f64(gate, x, N, K, threads=THREADS)
             silu = g64 / (1.0 + np.exp(-g64))
             tolerance.check(yv, y64 * silu, mag * np.abs(silu) + np.abs(y64) * 1.1 * mg, what)
+
+
+@pytest.mark.parametrize("B", [1, 2])
+@pytest.mark.parametrize("split", [2, 3, 5, 8, 9])
+@pytest.mark.parametrize("op", [q4rdna.OP_PLAIN, q4rdna.OP_SWIGLU])
+def test_cluster_reduction_matches_plan_reduction(cuda, B, split, op):
+    """A single call with 2..8 K-ranges adds them through distributed shared
+    memory inside one cluster per row block; a plan (and a single call with
+    more than 8) adds them through the workspace after an arrival ticket.
+    Both add the same partial sums in the same order, so the outputs must be
+    the same bits; and both must match the fp64 oracle.  The fused RMSNorm
+    rides along on the plain op."""
+    N, K = 1056, 4096  # 9 row blocks, the last one partial
+    tiles = synth.tiles_np(N, K, 8100 + split)
+    gate = synth.tiles_np(N, K, 8150 + split)
+    x = synth.x_np(K, B, 8200 + split)
+    g = (np.abs(synth.x_np(K, 1, 8250 + split)[0]) + 0.5).astype(np.float32)
+    td, gd = torch.from_numpy(tiles).to(cuda), torch.from_numpy(gate).to(cuda)
+    xd, gn = torch.from_numpy(x).to(cuda), torch.from_numpy(g).to(cuda)
+    kw = {"op": op, "split": split}
+    if op == q4rdna.OP_SWIGLU:
+        kw["gate_tiles"] = gd
+    norm = {"norm_weight": gn, "norm_eps": 1e-6} if op == q4rdna.OP_PLAIN else {}
+    single = q4rdna.gemv(td, xd, **kw, **norm).cpu().numpy()
+    y = torch.empty((B, N), device=cuda)
+    desc = {"tiles": td, "x": xd, "y": y, "op": op, "split": split}
+    if op == q4rdna.OP_SWIGLU:
+        desc["gate_tiles"] = gd
+    if norm:
+        desc.update(norm)
+    plan = q4rdna.Plan([desc], B=B)
+    plan.run()
+    planned = y.cpu().numpy()
+    plan.close()
+    assert np.array_equal(single.view(np.uint32), planned.view(np.uint32))
+    if norm:  # ggml's RMSNorm in fp64: h / sqrt(mean(h^2) + eps) * g
+        x64 = x.astype(np.float64)
+        xin = (x64 / np.sqrt(np.mean(x64 * x64, axis=1, keepdims=True) + 1e-6) * g.astype(np.float64)).astype(np.float32)
+    else:
+        xin = x
+    y64, mag = oracle.gemv_f64(tiles, xin, N, K, threads=THREADS)
+    if op == q4rdna.OP_SWIGLU:
+        g64, mg = oracle.gemv_f64(gate, x, N, K, threads=THREADS)
+        silu = g64 / (1.0 + np.exp(-g64))
+        tolerance.check(single, y64 * silu, mag * np.abs(silu) + np.abs(y64) * 1.1 * mg, f"swiglu split={split}")
+    else:
+        tolerance.check(single, y64, mag, f"rmsnorm split={split}")
