@@ -26,9 +26,9 @@
 // q4_tc_gemv_kernel: persistent, one CTA per SM, warp-specialised.  A work item
 //   is two "A-blocks" x one K-range of whole chunks: two 128-row blocks of a
 //   tensor, or, for SwiGLU, the up and the gate tiles of one row block.
-//   * warp 0 (one lane): cp.async.bulk copies of the raw tiles (per row tile,
-//     4 groups = 4352 contiguous bytes) and of the chunk's operand image into a
-//     ring of shared-memory stages, completion counted on mbarriers;
+//   * warp 0: cp.async.bulk copies of the raw tiles (per row tile, 4 groups =
+//     4352 contiguous bytes; one lane per copy) and of the chunk's operand image
+//     into a ring of shared-memory stages, completion counted on mbarriers;
 //   * warps 2..5: unpack.  A stored byte holds row r's columns 2i (low nibble)
 //     and 2i + 1 (high nibble); w & 0xF0F0F0F0 and (w << 4) & 0xF0F0F0F0 are
 //     exactly 16 * code as s8 for the odd and the even column.  The tile's
@@ -74,7 +74,6 @@ constexpr int kTcAPlane = 8 * kTcSlab;                   // 128 rows x 32 K
 constexpr int kTcABlock = 2 * kTcAPlane;                 // planes lo and hi
 constexpr int kTcAStage = kTcRA * kTcABlock;             // one group, both A-blocks
 constexpr int kTcFac = kTcCG * 16 * 4;                   // f32 factors [group][16 columns] per chunk
-constexpr int kTcSlots = 4;                              // TMEM accumulator slots (one group each)
 // warp roles: 0 copies, 1..3 MMA issue, 4..7 unpack, 8..23 epilogue (A-block x
 // half of the batch columns x TMEM lane quarter).  24 warps, six per SM
 // sub-partition (80 registers per thread).
@@ -94,13 +93,19 @@ struct Tc {
     static constexpr int IMG = 2 * IMGP;                 // a group's operand image
     static constexpr int CHUNK = kTcCG * IMG + kTcFac;   // a chunk of the prepared activation
     static constexpr int RAW = kTcRawW + CHUNK;          // one stage of the copy ring
-    static constexpr int NRAW = 3;
-    static constexpr int NA = 3;                         // unpacked A stages
-    static constexpr int TCOLS = kTcSlots * kTcRA * NCOL;  // 256 or 512 TMEM columns
+    static constexpr int NRAW = BP == 8 ? 3 : 2;         // raw stages in flight
+    // TMEM accumulator slots (one group each) and unpacked A stages.  The
+    // unpack warps reuse A stage n % NA after the MMAs of group n - NA, which
+    // they learn from that group's TMEM slot barrier: NA <= NSL keeps that
+    // barrier within one phase of the wait.
+    static constexpr int NSL = BP == 8 ? 8 : 4;
+    static constexpr int NA = BP == 8 ? 5 : 4;
+    static constexpr int TCOLS = NSL * kTcRA * NCOL;     // all 512 TMEM columns
+    static_assert(NA <= NSL, "A-stage reuse waits on the TMEM slot barrier");
     static constexpr int OFF_A = NRAW * RAW;
     static constexpr int OFF_X = OFF_A + NA * kTcAStage;  // SwiGLU gate sums [BP][128]
     static constexpr int OFF_BAR = OFF_X + BP * Q4_BLOCK_ROWS * 4;
-    static constexpr int NBAR = 2 * NRAW + NA + 2 * kTcSlots + 2 * kTcMmaWarps + 1;
+    static constexpr int NBAR = 2 * NRAW + NA + 2 * NSL + 2 * kTcMmaWarps + 1;
     static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // TMEM address, last-CTA flag, norm scales
     static constexpr int SMEM = OFF_MISC + 16 + BP * 4;
     // instruction descriptor: D s32, A and B s8, both MN-major, N = NCOL, M = 128
@@ -317,7 +322,7 @@ __global__ void __launch_bounds__(128) q4_tc_prep_kernel(const __grid_constant__
 template <int BP, bool HAS_DUAL>
 __global__ void __launch_bounds__(kTcThreads, 1) q4_tc_gemv_kernel(const __grid_constant__ Launch L) {
     using S = Tc<BP>;
-    constexpr int NCOL = S::NCOL, NRAW = S::NRAW, NA = S::NA, NSL = kTcSlots;
+    constexpr int NCOL = S::NCOL, NRAW = S::NRAW, NA = S::NA, NSL = S::NSL;
     extern __shared__ __align__(1024) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint8_t *raw = smem;
@@ -396,17 +401,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_tc_gemv_kernel(const __grid_
     bool ok = true;
     if (warp == 0) {
         // ---------------------------------------------------------- producer
-        if (lane == 0) {
-            uint32_t rit = 0;
-            bool waited = false;
-            for (long long it = blockIdx.x; ok && it < L.total_items; it += gridDim.x) {
-                const TcItem I = tc_item<HAS_DUAL>(L, it);
-                const Task &T = *I.T;
-                const int rtiles = T.N / Q4_TILE_ROWS;
-                for (int g = I.g0; g < I.g1; g += kTcCG, ++rit) {
-                    const int ng = min(kTcCG, I.g1 - g);
-                    const int s = rit % NRAW;
-                    if (!mbar_wait(raw_empty(s), ((rit / NRAW) & 1u) ^ 1u)) { ok = false; break; }
+        // The whole warp walks the chunks; lanes 0..7 issue the 8 tile-run
+        // copies of a chunk and lane 8 its operand image, so that the copies of
+        // a chunk are issued at once (one thread spends a few hundred cycles per
+        // cp.async.bulk and cannot keep up with the stream on its own).
+        uint32_t rit = 0;
+        bool waited = false;
+        for (long long it = blockIdx.x; ok && it < L.total_items; it += gridDim.x) {
+            const TcItem I = tc_item<HAS_DUAL>(L, it);
+            const Task &T = *I.T;
+            const int rtiles = T.N / Q4_TILE_ROWS;
+            for (int g = I.g0; g < I.g1; g += kTcCG, ++rit) {
+                const int ng = min(kTcCG, I.g1 - g);
+                const int s = rit % NRAW;
+                bool free_stage = true;
+                if (lane == 0) free_stage = mbar_wait(raw_empty(s), ((rit / NRAW) & 1u) ^ 1u);
+                if (!__shfl_sync(0xffffffffu, free_stage, 0)) { ok = false; break; }
+                const uint32_t dst = smem_u32(raw + (size_t)s * S::RAW);
+                if (lane == 0) {
                     uint32_t bytes = S::CHUNK;
                     for (int a = 0; a < I.nab; ++a) {
                         const int rb = I.dual ? I.rb0 : I.rb0 + a;
@@ -414,18 +426,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_tc_gemv_kernel(const __grid_
                             if (rb * Q4_BLOCK_TILES + t < rtiles) bytes += (uint32_t)ng * Q4_TILE_BYTES;
                     }
                     mbar_expect_tx(raw_full(s), bytes);
-                    const uint32_t dst = smem_u32(raw + (size_t)s * S::RAW);
-                    for (int a = 0; a < I.nab; ++a) {
-                        const int rb = I.dual ? I.rb0 : I.rb0 + a;
-                        const uint8_t *w = (I.dual && a == 1) ? T.w2 : T.w;
-                        for (int t = 0; t < Q4_BLOCK_TILES; ++t) {
-                            const int rt = rb * Q4_BLOCK_TILES + t;
-                            if (rt >= rtiles) break;
-                            bulk_g2s(dst + (uint32_t)((a * Q4_BLOCK_TILES + t) * kTcSpan),
-                                     w + ((size_t)rt * T.G + g) * Q4_TILE_BYTES, (uint32_t)ng * Q4_TILE_BYTES,
-                                     raw_full(s));
-                        }
-                    }
+                }
+                __syncwarp();
+                if (lane < kTcRA * Q4_BLOCK_TILES) {
+                    const int a = lane >> 2, t = lane & 3;
+                    const int rb = I.dual ? I.rb0 : I.rb0 + a;
+                    const int rt = rb * Q4_BLOCK_TILES + t;
+                    if (a < I.nab && rt < rtiles)
+                        bulk_g2s(dst + (uint32_t)((a * Q4_BLOCK_TILES + t) * kTcSpan),
+                                 ((I.dual && a == 1) ? T.w2 : T.w) + ((size_t)rt * T.G + g) * Q4_TILE_BYTES,
+                                 (uint32_t)ng * Q4_TILE_BYTES, raw_full(s));
+                } else if (lane == kTcRA * Q4_BLOCK_TILES) {
                     if (!waited) {  // the operand image is written by the prep kernel
                         asm volatile("griddepcontrol.wait;" ::: "memory");
                         waited = true;
@@ -433,11 +444,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_tc_gemv_kernel(const __grid_
                     bulk_g2s(dst + kTcRawW, T.img + (size_t)(g / kTcCG) * S::CHUNK, S::CHUNK, raw_full(s));
                 }
             }
-            if (!ok) atomicOr(&g_fault, kFaultTileWait);
-            // no copy may still be landing when the CTA leaves
+        }
+        if (!ok && lane == 0) atomicOr(&g_fault, kFaultTileWait);
+        // no copy may still be landing when the CTA leaves
+        if (lane == 0)
             for (uint32_t k = rit > (uint32_t)NRAW ? rit - NRAW : 0; k < rit; ++k)
                 mbar_wait(raw_full(k % NRAW), (k / NRAW) & 1u);
-        }
     } else if (warp < kTcUnpackWarp0) {
         // ---------------------------------------------------------- MMA issue (warp 1 + j: groups n % kTcMmaWarps == j)
         const int j = warp - kTcMmaWarp0;
