@@ -27,9 +27,10 @@
 //   is two "A-blocks" x one K-range of whole chunks: two 128-row blocks of a
 //   tensor, or, for SwiGLU, the up and the gate tiles of one row block.
 //   * warp 0: cp.async.bulk copies of the raw tiles (per row tile, 4 groups =
-//     4352 contiguous bytes; one lane per copy) and of the chunk's operand image
-//     into a ring of shared-memory stages, completion counted on mbarriers;
-//   * warps 2..5: unpack.  A stored byte holds row r's columns 2i (low nibble)
+//     4352 contiguous bytes; lanes 0..7 one copy each) and of the chunk's
+//     operand image (lane 8) into a ring of shared-memory stages, completion
+//     counted on mbarriers;
+//   * warps 4..7: unpack.  A stored byte holds row r's columns 2i (low nibble)
 //     and 2i + 1 (high nibble); w & 0xF0F0F0F0 and (w << 4) & 0xF0F0F0F0 are
 //     exactly 16 * code as s8 for the odd and the even column.  The tile's
 //     bytes for pair column i and rows 16h..16h+15 are 16 contiguous bytes, so
@@ -37,26 +38,25 @@
 //     planes (128 rows x 32 K): byte (m, i) at m % 16 + 16 (i % 8) + 128 (i / 8)
 //     + 576 (m / 16).  The 576-byte stride of a 16-row slab (512 + 64) keeps
 //     both the loads and the stores free of bank conflicts;
-//   * warp 1 (one lane): per group and A-block two MMAs, M = 128, N = 4 BP,
-//     K = 32 (plane lo, then plane hi), into a TMEM slot that already holds the
-//     bias 0x4B400000 in every word.  The int32 sums of a group stay below 2^22
-//     in magnitude, so each accumulator word, read as an f32, is exactly
-//     1.5 * 2^23 + S;
-//   * warps 6..13: epilogue, one TMEM lane (= one row) per thread, warps 6..9
-//     for A-block 0 and 10..13 for A-block 1 (a warp reaches the TMEM lanes
-//     32 (warp % 4) ..).  Per group: tcgen05.ld of the row's 4 BP words (32 at
-//     a time), the bias written back with tcgen05.st (the slot is then ready
-//     for the next group), the digit sums recombined as ((S3 256 + S2) 256 + S1) 256 + S0
-//     and accumulated with the row's fp16 scale / 16; per chunk the sum is
-//     multiplied by the chunk's factor 2^(E - 156).
+//   * warps 1..3 (one lane each, group n on warp 1 + n % 3): per group and
+//     A-block two MMAs, M = 128, N = 4 BP, K = 32 (plane lo, then plane hi),
+//     into a TMEM slot that already holds the bias 0x4B400000 in every word.
+//     The int32 sums of a group stay below 2^22 in magnitude, so each
+//     accumulator word, read as an f32, is exactly 1.5 * 2^23 + S;
+//   * warps 8..23: epilogue, one TMEM lane (= one row) per thread: 2 A-blocks
+//     x 2 halves of the batch columns x 4 lane quarters (a warp reaches the
+//     TMEM lanes 32 (warp % 4) ..).  Per group: tcgen05.ld of the row's words,
+//     the bias written back with tcgen05.st (the slot is then ready for the
+//     next group), the digit sums recombined as ((S3 256 + S2) 256 + S1) 256
+//     + S0 and accumulated with fma(scale / 16, X * 2^(E - 156), acc), the
+//     factor 2^(E - 156) being the (group, column) one of the prepared image.
 //
 // Accumulation order of an output: exact int32 per (group, digit); digits
-// combined in f32 (three roundings); groups of a chunk ascending with
-// fma(scale / 16, X, s); chunks of a K-range ascending with fma(s, factor,
-// acc); K-ranges of a split row block ascending (last CTA to arrive).  The
-// tolerance against the fp64 oracle is the suite's normwise bound; the order
-// is not the reference's CPU order, which a tensor-core contraction cannot
-// keep.
+// combined in f32 (three roundings); groups of a K-range ascending with
+// fma(scale / 16, X * factor, acc); K-ranges of a split row block ascending
+// (last CTA to arrive).  The tolerance against the fp64 oracle is the
+// suite's normwise bound; the order is not the reference's CPU order, which
+// a tensor-core contraction cannot keep.
 //
 // Synchronisation: every wait is bounded (about one second, %globaltimer);
 // on expiry the waiting role sets bit 2 of the fault flag
