@@ -492,6 +492,11 @@ def build_step(model: str, rank: int, world: int, device, seed: int, layers: int
     names = synth.model_tensors(model)
     if layers:
         names = [t for t in names if int(t[0].split(".")[1]) < layers]
+    if hybrid:
+        # the Q4_K tensors' activations and outputs first: one byte range each
+        # way, disjoint from the Q4_RDNA segments', so that run_host overlaps
+        # the Q4_K launch and its copies with the Q4_RDNA segments
+        names = sorted(names, key=lambda t: 0 if any(q in t[0] for q in QKV) else 1)
     try:
         lay = tp.Layout(names, world, B=B)
     except ValueError as e:

@@ -243,6 +243,13 @@ void q4rdna_plan_destroy(q4rdna_plan *plan);
  * The first call with a given set of buffers does the capture; make it outside
  * any stream capture of the caller.  The
  * segments' activation ranges must not overlap, nor their output ranges.
+ * Q4_K descriptors (Q4RDNA_FORMAT_Q4K) form one more segment: their
+ * activations are copied in first, their launch runs beside the first Q4_RDNA
+ * segment and their outputs are copied out (never stored straight into
+ * y_host).  When the Q4_K descriptors' byte range of activations or of
+ * outputs meets a Q4_RDNA segment's, the call instead copies all of x in,
+ * runs the plan and copies all of y out; placing the Q4_K tensors' inputs and
+ * outputs apart (say first in both buffers) keeps the overlap.
  * With a fused gather (q4rdna_plan_set_gather) the segments also store into
  * every rank's gathered buffer and the run ends with the flag exchange; y_host
  * then receives this rank's outputs (its y buffer), and the calls are direct

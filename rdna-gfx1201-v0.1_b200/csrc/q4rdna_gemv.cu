@@ -819,6 +819,14 @@ struct q4rdna_plan {
     std::vector<q4k::Task> q4k_host;
     q4k::Task *q4k_table = nullptr;
     long long q4k_items = 0;
+    // q4rdna_plan_run_host with Q4_K tasks: their launch is one more segment,
+    // with its own input copy (first on the copy stream) and output copy,
+    // beside the Q4_RDNA segments
+    struct KSeg {
+        bool on = false;
+        size_t x_lo = 0, x_hi = 0, y_lo = 0, y_hi = 0;  // byte ranges from x_dev / y_dev
+        cudaEvent_t x_ready = nullptr, y_ready = nullptr;
+    } kseg;
 };
 
 namespace {
@@ -1292,6 +1300,32 @@ q4rdna_status build_segments(q4rdna_plan *p, int want, const uint8_t *xd, size_t
         }
         first = last;
     }
+    // the Q4_K tasks of a run_host plan: one segment of their own
+    p->kseg.on = false;
+    if (xd != nullptr && !p->q4k_host.empty()) {
+        auto &k = p->kseg;
+        k.x_lo = k.y_lo = SIZE_MAX;
+        k.x_hi = k.y_hi = 0;
+        for (const q4k::Task &T : p->q4k_host) {
+            const uint8_t *x = reinterpret_cast<const uint8_t *>(T.x);
+            const uint8_t *y = reinterpret_cast<const uint8_t *>(T.y);
+            const size_t xn = (size_t)p->B * T.K * sizeof(float), yn = (size_t)p->B * T.N * sizeof(float);
+            if (x < xd || x + xn > xd + xb || y < yd || y + yn > yd + yb) return Q4RDNA_ERR_INVALID_ARGUMENT;
+            k.x_lo = std::min(k.x_lo, (size_t)(x - xd));
+            k.x_hi = std::max(k.x_hi, (size_t)(x - xd) + xn);
+            k.y_lo = std::min(k.y_lo, (size_t)(y - yd));
+            k.y_hi = std::max(k.y_hi, (size_t)(y - yd) + yn);
+        }
+        if ((k.x_ready == nullptr && cudaEventCreateWithFlags(&k.x_ready, cudaEventDisableTiming) != cudaSuccess) ||
+            (k.y_ready == nullptr && cudaEventCreateWithFlags(&k.y_ready, cudaEventDisableTiming) != cudaSuccess))
+            return Q4RDNA_ERR_CUDA;
+        // ranges shared with a Q4_RDNA segment (say q/k/v in Q4_K reading the
+        // same x as a Q4_RDNA tensor) cannot overlap: run_host then copies in,
+        // runs and copies out the whole plan
+        k.on = true;
+        for (const auto &sg : p->segs)
+            if ((k.x_lo < sg.x_hi && sg.x_lo < k.x_hi) || (k.y_lo < sg.y_hi && sg.y_lo < k.y_hi)) k.on = false;
+    }
     // the segments' ranges must be disjoint: a later segment's input copy may
     // land while an earlier segment still reads, and outputs leave early
     for (size_t a = 0; xd != nullptr && a < p->segs.size(); ++a)
@@ -1337,13 +1371,31 @@ q4rdna_status launch_segments(q4rdna_plan *plan, cudaStream_t cs, const uint8_t 
         cudaStreamWaitEvent(plan->comp[1], plan->start, 0) != cudaSuccess)
         return Q4RDNA_ERR_CUDA;
     const bool out_copies = copies && !plan->seg_direct;  // direct: the kernels store into yh
+    const bool kseg = copies && plan->kseg.on;  // the Q4_K tasks' segment (copies both ways)
     if (copies && cudaStreamWaitEvent(plan->h2d, plan->start, 0) != cudaSuccess) return Q4RDNA_ERR_CUDA;
-    if (out_copies && cudaStreamWaitEvent(plan->d2h, plan->start, 0) != cudaSuccess) return Q4RDNA_ERR_CUDA;
+    if ((out_copies || kseg) && cudaStreamWaitEvent(plan->d2h, plan->start, 0) != cudaSuccess) return Q4RDNA_ERR_CUDA;
+    if (kseg) {  // its inputs first: the Q4_K kernel then runs beside the first Q4_RDNA segment
+        const auto &k = plan->kseg;
+        if (cudaMemcpyAsync(xd + k.x_lo, xh + k.x_lo, k.x_hi - k.x_lo, cudaMemcpyHostToDevice, plan->h2d) !=
+                cudaSuccess ||
+            cudaEventRecord(k.x_ready, plan->h2d) != cudaSuccess)
+            return Q4RDNA_ERR_CUDA;
+    }
     for (auto &sg : plan->segs) {
         if (!copies) break;
         if (cudaMemcpyAsync(xd + sg.x_lo, xh + sg.x_lo, sg.x_hi - sg.x_lo, cudaMemcpyHostToDevice, plan->h2d) !=
                 cudaSuccess ||
             cudaEventRecord(sg.x_ready, plan->h2d) != cudaSuccess)
+            return Q4RDNA_ERR_CUDA;
+    }
+    if (kseg) {
+        const auto &k = plan->kseg;
+        cudaStream_t c = plan->comp[1];
+        if (cudaStreamWaitEvent(c, k.x_ready, 0) != cudaSuccess) return Q4RDNA_ERR_CUDA;
+        const q4rdna_status st = launch_q4k(plan, c);
+        if (st != Q4RDNA_OK) return st;
+        if (cudaEventRecord(k.y_ready, c) != cudaSuccess || cudaStreamWaitEvent(plan->d2h, k.y_ready, 0) != cudaSuccess ||
+            cudaMemcpyAsync(yh + k.y_lo, yd + k.y_lo, k.y_hi - k.y_lo, cudaMemcpyDeviceToHost, plan->d2h) != cudaSuccess)
             return Q4RDNA_ERR_CUDA;
     }
     for (size_t i = 0; i < plan->segs.size(); ++i) {
@@ -1367,10 +1419,11 @@ q4rdna_status launch_segments(q4rdna_plan *plan, cudaStream_t cs, const uint8_t 
                 cudaSuccess)
             return Q4RDNA_ERR_CUDA;
     }
-    if (out_copies) {
+    if (out_copies || kseg) {  // every output copy is on the copy-out stream
         if (cudaEventRecord(plan->done, plan->d2h) != cudaSuccess || cudaStreamWaitEvent(cs, plan->done, 0) != cudaSuccess)
             return Q4RDNA_ERR_CUDA;
-    } else {
+    }
+    if (!out_copies) {
         // the last segment of each stream ends that stream's work
         const size_t n = plan->segs.size();
         for (size_t i = n >= 2 ? n - 2 : 0; i < n; ++i)
@@ -1391,8 +1444,7 @@ q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *
         return Q4RDNA_ERR_INVALID_ARGUMENT;
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev != plan->device) return Q4RDNA_ERR_DEVICE;
-    if (!plan->q4k_host.empty()) {
-        // plans with Q4_K tensors: one copy in, the run, one copy out (not overlapped)
+    auto whole = [&]() -> q4rdna_status {  // one copy in, the run, one copy out
         cudaStream_t cs = (cudaStream_t)stream;
         if (cudaMemcpyAsync(x_dev, x_host, x_bytes, cudaMemcpyHostToDevice, cs) != cudaSuccess)
             return Q4RDNA_ERR_CUDA;
@@ -1401,7 +1453,8 @@ q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *
         if (cudaMemcpyAsync(y_host, y_dev, y_bytes, cudaMemcpyDeviceToHost, cs) != cudaSuccess)
             return Q4RDNA_ERR_CUDA;
         return Q4RDNA_OK;
-    }
+    };
+    if (!plan->q4k_host.empty() && plan->count == 0) return whole();  // Q4_K tensors only
     const int want = segments != 0 ? segments
                                    : (direct_batch(plan->B) && mapped_output(y_host, y_bytes) != nullptr ? kHostSegmentsDirect
                                                                                                           : kHostSegments);
@@ -1414,7 +1467,9 @@ q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *
     } else {
         for (const auto &sg : plan->segs)
             if (sg.x_hi > x_bytes || sg.y_hi > y_bytes) return Q4RDNA_ERR_INVALID_ARGUMENT;
+        if (plan->kseg.on && (plan->kseg.x_hi > x_bytes || plan->kseg.y_hi > y_bytes)) return Q4RDNA_ERR_INVALID_ARGUMENT;
     }
+    if (!plan->q4k_host.empty() && !plan->kseg.on) return whole();  // Q4_K ranges shared with Q4_RDNA ones
     if (plan->gather) {
         // a gather plan: the segments store into every rank's gathered buffer
         // (and the host buffer when it is mapped), then the flag exchange; the
@@ -1442,12 +1497,14 @@ q4rdna_status q4rdna_plan_run_host(q4rdna_plan *plan, const void *x_host, void *
         if (plan->cap == nullptr && cudaStreamCreateWithFlags(&plan->cap, cudaStreamNonBlocking) != cudaSuccess)
             return Q4RDNA_ERR_CUDA;
         if (cudaStreamBeginCapture(plan->cap, cudaStreamCaptureModeRelaxed) != cudaSuccess) return Q4RDNA_ERR_CUDA;
-        const uint64_t before = g_launches.load();
+        const uint64_t before = g_launches.load(), before_k = q4k_launch_count();
         const q4rdna_status st = launch_segments(plan, plan->cap, static_cast<const uint8_t *>(x_host),
                                                  static_cast<uint8_t *>(x_dev), static_cast<const uint8_t *>(y_dev),
                                                  static_cast<uint8_t *>(y_host));
-        const uint64_t captured = g_launches.load() - before;
-        g_launches.fetch_sub(captured, std::memory_order_relaxed);  // counted per replay below
+        // launches recorded by the capture are counted per replay below (the
+        // Q4_K counter's share comes off this one: the sum stays exact)
+        const uint64_t captured = (g_launches.load() - before) + (q4k_launch_count() - before_k);
+        g_launches.fetch_sub(captured, std::memory_order_relaxed);
         cudaGraph_t g = nullptr;
         const cudaError_t ec = cudaStreamEndCapture(plan->cap, &g);
         if (st != Q4RDNA_OK || ec != cudaSuccess || g == nullptr) {
@@ -1566,6 +1623,8 @@ void q4rdna_plan_destroy(q4rdna_plan *plan) {
     for (cudaStream_t c : plan->comp)
         if (c) cudaStreamDestroy(c);
     if (plan->d2h) cudaStreamDestroy(plan->d2h);
+    if (plan->kseg.x_ready) cudaEventDestroy(plan->kseg.x_ready);
+    if (plan->kseg.y_ready) cudaEventDestroy(plan->kseg.y_ready);
     if (plan->start) cudaEventDestroy(plan->start);
     if (plan->done) cudaEventDestroy(plan->done);
     for (Task *t : plan->gtable)

@@ -196,3 +196,68 @@ def test_q4k_only_plan_and_run_host(cuda):
     torch.cuda.current_stream().synchronize()
     assert np.array_equal(y_host.numpy().view(np.uint32), want)
     plan.close()
+
+
+def _host_step(cuda, B, shared_x, seed):
+    """Two Qwen3-8B-shaped layers of the qkv-fallback hybrid with every input
+    and output in one device buffer each (run_host's contract).  The Q4_K
+    tensors (q, k, v, reading one x per layer) come first in both buffers;
+    with shared_x the Q4_RDNA attn_output reads layer 0's q/k/v input too, so
+    the Q4_K ranges meet a Q4_RDNA segment's."""
+    layers = [[(n, N, K) for (n, N, K) in synth.QWEN3_8B_LAYER] for _ in range(2)]
+    qkv = [(L, t) for L in range(2) for t in layers[L] if t[0].split(".")[0] in ("attn_q", "attn_k", "attn_v")]
+    rest = [(L, t) for L in range(2) for t in layers[L] if t[0].split(".")[0] not in ("attn_q", "attn_k", "attn_v")]
+    xs, ys = {}, {}
+    xo = yo = 0
+    for L, (name, N, K) in qkv + rest:
+        key = ("qkv", L) if (L, name) in [(a, b[0]) for a, b in qkv] else (L, name)
+        if key not in xs:
+            xs[key] = xo
+            xo += B * K
+        ys[(L, name)] = yo
+        yo += B * N
+    x_dev = torch.empty(xo, dtype=torch.float32, device=cuda)
+    y_dev = torch.empty(yo, dtype=torch.float32, device=cuda)
+    descs = []
+    for i, (L, (name, N, K)) in enumerate(qkv + rest):
+        seed_i = seed + 10 * L + i
+        is_q4k = (L, name) in [(a, b[0]) for a, b in qkv]
+        key = ("qkv", L) if is_q4k else (L, name)
+        if shared_x and name == "attn_output.weight" and L == 0:
+            key = ("qkv", 0)
+        xoff = xs[key]
+        d = {"x": x_dev[xoff:xoff + B * K].view(B, K), "y": y_dev[ys[(L, name)]:ys[(L, name)] + B * N].view(B, N)}
+        if is_q4k:
+            d.update(tiles=to_dev(synth.q4k_np(N, K, seed_i), cuda), format=q4rdna.FORMAT_Q4K)
+        else:
+            d["tiles"] = to_dev(synth.tiles_np(N, K, seed_i), cuda)
+            if name == "ffn_gate.weight":
+                d.update(op=q4rdna.OP_SWIGLU, gate_tiles=to_dev(synth.tiles_np(N, K, seed_i + 1), cuda))
+        descs.append(d)
+    x_host = torch.from_numpy(np.random.default_rng(seed).standard_normal(xo, dtype=np.float32)).pin_memory()
+    return q4rdna.Plan(descs, B=B), x_dev, y_dev, x_host, yo
+
+
+@pytest.mark.parametrize("B", [1, 4])
+@pytest.mark.parametrize("shared_x", [False, True])
+def test_hybrid_run_host_equals_copies_and_run(cuda, B, shared_x):
+    """run_host on a plan mixing Q4_K and Q4_RDNA tensors: the Q4_K launch and
+    its copies run as one more segment beside the Q4_RDNA segments (or, when
+    their byte ranges meet, the whole plan is copied in, run and copied out).
+    Either way the outputs are exactly those of copy-in, run, copy-out, into a
+    pinned (mapped) or a pageable output buffer, call after call."""
+    plan, x_dev, y_dev, x_host, ny = _host_step(cuda, B, shared_x, 9400 + B)
+    x_dev.copy_(x_host)
+    plan.run()
+    want = y_dev.cpu().numpy().view(np.uint32).copy()
+    for y_host in (torch.empty(ny, dtype=torch.float32).pin_memory(), torch.empty(ny, dtype=torch.float32)):
+        for segments in (0, 3):
+            for rep in range(2):
+                x_dev.zero_()
+                y_dev.fill_(float("nan"))
+                y_host.fill_(float("nan"))
+                plan.run_host(x_host, x_dev, y_dev, y_host, segments=segments)
+                torch.cuda.current_stream().synchronize()
+                assert np.array_equal(y_host.numpy().view(np.uint32), want), (segments, rep)
+    plan.close()
+    assert q4rdna.take_fault() == 0
