@@ -85,6 +85,38 @@ def main() -> int:
                 bad += 1
         dist.barrier()
         pg.close()
+        # dependent stages: two gather plans (the first tensors, the rest) run by
+        # one q4rdna_plan_run_many call, which captures the pair once per run
+        # parity and replays it, the flag exchange counting its epochs on the
+        # device; four calls fill both gathered buffers twice
+        stage_plans, pgs, wants = [], [], []
+        for part in (TENSORS[:2], TENSORS[2:]):
+            slay = tp.Layout(part, world, B)
+            ys = torch.zeros(B * slay.ysz, dtype=torch.float32, device=dev)
+            idx = [TENSORS.index(t) for t in part]
+            sd = [{"tiles": descs[i]["tiles"], "x": descs[i]["x"], "y": slay.local_view(ys, k)}
+                  for k, i in enumerate(idx)]
+            sp = q4rdna.Plan(sd, B=B)
+            sp.run()
+            g = torch.empty(world * B * slay.ysz, dtype=torch.float32, device=dev)
+            tp.all_gather(ys, g)
+            torch.cuda.synchronize()
+            wants.append(g.cpu().numpy().view(np.uint32).copy())
+            pgs.append(tp.PeerGather(sp, slay, ys))
+            stage_plans.append(sp)
+        for run in range(4):
+            q4rdna.run_plans(stage_plans)
+            torch.cuda.synchronize()
+            for k, (sp, spg) in enumerate(zip(stage_plans, pgs)):
+                par = spg._lib.q4rdna_plan_gather_parity(sp._h)
+                if not np.array_equal(spg.gathered[par].cpu().numpy().view(np.uint32), wants[k]):
+                    print(f"rank {rank} B={B} run_many call {run} stage {k}: fused gather differs", flush=True)
+                    bad += 1
+        dist.barrier()
+        for spg in pgs:
+            spg.close()
+        for sp in stage_plans:
+            sp.close()
         plan.close()
         fault = q4rdna.take_fault()
         if fault:
