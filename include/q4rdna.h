@@ -81,7 +81,10 @@ const char *q4rdna_version(void);
 int q4rdna_select_split(int N, int K, int B, int op);
 
 /* Device workspace a single GEMV needs: split-K partial sums plus arrival
- * tickets (0 when the chosen split is 1 and B < 8), and at B >= 8 (the
+ * tickets (0 when the chosen split is 1 and B < 8, and at B <= 2 for splits
+ * up to 8, whose K-ranges meet in a thread-block cluster: the default
+ * selector's choice, so the name-keyed operators allocate nothing per stream
+ * unless LLAMA_Q4_RDNA_COOP forces a larger split), and at B >= 8 (the
  * tensor-core tile path) also the activation prepared for the tensor cores
  * (4 bytes per element of x, plus a small per-chunk table).  A workspace must
  * be zero-filled once when it is allocated (q4rdna_workspace_init); every call

@@ -417,7 +417,13 @@ size_t ws_split_bytes(int N, int B, int S, int op) {
 size_t ws_prep_offset(int N, int B, int S, int op) {
     return align256(S <= 1 ? kTicketArea : ws_split_bytes(N, B, S, op));
 }
+// A single call at B < kTileMinBatch with 2..kMaxClusterSplit K-ranges runs
+// as thread-block clusters that add their K-ranges in distributed shared
+// memory (launch_cta): no tickets, no partial sums, no workspace.
+bool cluster_call(int B, int S) { return B < kTileMinBatch && S > 1 && S <= kMaxClusterSplit; }
+
 size_t ws_bytes_for(int N, int K, int B, int S, int op) {
+    if (cluster_call(B, S)) return 0;
     if (B < kTcMinBatch) return ws_split_bytes(N, B, S, op);
     return ws_prep_offset(N, B, S, op) + tc_prep_bytes(K, B, true);
 }
@@ -583,7 +589,7 @@ q4rdna_status gemv_common(int op, const uint8_t *w, const uint8_t *w2, const flo
     unsigned *ticket = nullptr;
     float *part = nullptr;
     uint8_t *prep = nullptr;
-    if (sp.S > 1 || tc) {
+    if ((sp.S > 1 && !cluster_call(B, sp.S)) || tc) {
         const size_t need = ws_bytes_for(N, K, B, sp.S, op);
         if (ws == nullptr || ws_bytes < need || !aligned(ws, 256)) return Q4RDNA_ERR_WORKSPACE;
         if (sp.S > 1) {

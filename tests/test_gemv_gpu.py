@@ -153,7 +153,10 @@ def test_error_statuses_on_device(cuda):
     assert L.q4rdna_gemv(tiles.data_ptr() + 8, x.data_ptr(), y.data_ptr(), N, K, 1, None, None, 0, st) == 3
     assert L.q4rdna_gemv(tiles.data_ptr(), x.data_ptr() + 4, y.data_ptr(), N, K, 1, None, None, 0, st) == 3
     cfg = q4rdna.Cfg()
-    cfg.split = 4
+    cfg.split = 4  # K-ranges added inside a thread-block cluster: no workspace
+    assert L.q4rdna_workspace_bytes(N, K, 1, 0, ctypes.byref(cfg)) == 0
+    assert L.q4rdna_gemv(tiles.data_ptr(), x.data_ptr(), y.data_ptr(), N, K, 1, ctypes.byref(cfg), None, 0, st) == 0
+    cfg.split = 16  # beyond a cluster: partial sums and arrival tickets in the workspace
     need = L.q4rdna_workspace_bytes(N, K, 1, 0, ctypes.byref(cfg))
     assert need > 0
     ws = torch.zeros(need, dtype=torch.uint8, device=cuda)
@@ -280,9 +283,10 @@ def test_shared_workspace_across_shapes(cuda):
     L = q4rdna.lib
     st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     cfg = q4rdna.Cfg()
-    cfg.split = 2
+    cfg.split = 16  # more K-ranges than a cluster holds: the workspace path
     shapes = [(4096, 12288), (12288, 4096), (1024, 4096), (25600, 5120)]
     need = max(L.q4rdna_workspace_bytes(N, K, 1, 0, ctypes.byref(cfg)) for N, K in shapes)
+    assert need > 0
     ws = torch.zeros(need, dtype=torch.uint8, device=cuda)
     for rep in range(2):
         for i, (N, K) in enumerate(shapes):

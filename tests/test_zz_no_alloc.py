@@ -47,7 +47,12 @@ def _no_alloc(td, xd, N, K, B):
 def test_no_alloc_matches_workspace_entry_point_on_two_calls(cuda):
     # Two calls in a row share the scratch: the second (a different shape, with
     # more row blocks) must not see the first call's partial sums.
-    cases = [(4096, 12288, 1, 11), (12288, 4096, 2, 12), (12288, 4096, 2, 12)]
+    # Single calls at B <= 2 whose K-ranges meet in a thread-block cluster need
+    # no scratch at all; B = 8 (the tensor-core path) always uses it, for the
+    # prepared activation, so the last two calls exercise the shared array.
+    cases = [(4096, 12288, 1, 11), (12288, 4096, 2, 12), (12288, 4096, 8, 13), (4096, 4096, 8, 14)]
+    used = [q4rdna.lib.q4rdna_workspace_bytes(N, K, B, q4rdna.OP_PLAIN, None) for N, K, B, _ in cases]
+    assert used[2] > 0 and used[3] > 0
     for N, K, B, seed in cases:
         tiles = synth.tiles_np(N, K, seed)
         x = synth.x_np(K, B, seed + 100)
